@@ -1,0 +1,1213 @@
+// Host runtime of the B200 backend: weight upload, per-device workspaces,
+// the packed forward (BERT / XLM-R encoder and Qwen decoder families), the
+// multi-GPU sharder and the C ABI of include/ffwd_b200.h.
+//
+// Reference counterparts (libffwd/cuda.cu): weight upload 249-400 and
+// cuda_ctx_from_model 4212-4304; workspace growth ensure_buffers 3884-4125;
+// input upload cuda_upload_packed_inputs 4433-4500; Qwen forward
+// cuda_forward_batch 4975-5100; BERT forward cuda_forward_batch_bert
+// 4634-4973; encode entry points 5102-5225.  The reference drives one GPU; the
+// device set and the LPT sharder below have no counterpart there.
+#include "../../include/ffwd_b200.h"
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "loader.h"
+#include "ptx.cuh"
+#include "rowops.cuh"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <string>
+#include <thread>
+#include <vector>
+
+namespace fb {
+namespace {
+
+// ------------------------------------------------------------------ globals
+
+std::atomic<long long> g_launches{0};
+int g_gemm_mode = 0;         // 0 f32, 1 tf32, 2 bf16, 3 16f (reference default: f32)
+int g_weight_override = -1;  // -1 file dtype, 0 f32, 1 bf16, 2 f16
+std::vector<int> g_devices;
+bool g_devices_set = false;
+int g_max_tokens = 65536;
+thread_local std::string t_err;
+
+void fail(const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    fprintf(stderr, "ffwd_b200: %s\n", buf);
+}
+
+#define CK(expr)                                                                              \
+    do {                                                                                      \
+        cudaError_t _e = (cudaError_t)(expr);                                                 \
+        if (_e != cudaSuccess) {                                                              \
+            fail("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, __LINE__); \
+            return -1;                                                                        \
+        }                                                                                     \
+    } while (0)
+
+// Kernel launch wrappers return a cudaError_t value; count every launch.
+#define LAUNCH(expr)             \
+    do {                         \
+        g_launches.fetch_add(1); \
+        CK(expr);                \
+    } while (0)
+
+// ------------------------------------------------------------------ tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 row-major matrix [rows, cols]; box = box_rows x box_cols.
+int make_map(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+             uint32_t box_cols, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        fail("cuTensorMapEncodeTiled unavailable");
+        return -1;
+    }
+    if (rows == 0) rows = 1;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        fail("cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u", (int)r,
+             (unsigned long long)rows, (unsigned long long)cols, box_rows, box_cols);
+        return -1;
+    }
+    return 0;
+}
+
+// ------------------------------------------------------------------ model state
+
+struct Mat {
+    __nv_bfloat16 *hi = nullptr;
+    __nv_bfloat16 *lo = nullptr;  // 3-pass mode only
+    int rows = 0, cols = 0, bn = 128;
+    CUtensorMap map_hi, map_lo;
+};
+
+struct LayerW {
+    Mat qkv, o, up, down;  // up: fused interleaved [gate; up] (Qwen) or intermediate (BERT)
+    float *b_qkv = nullptr, *b_o = nullptr, *b_up = nullptr, *b_down = nullptr;
+    float *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+    float *ln1_g = nullptr, *ln1_b = nullptr, *ln2_g = nullptr, *ln2_b = nullptr;
+    int swiglu_half = 128;
+};
+
+struct Workspace {
+    int cap_t = 0, cap_b = 0, cap_items = 0, cap_spans = 0;
+    int *ids = nullptr, *pos = nullptr, *offsets = nullptr, *err = nullptr;
+    int *span_starts = nullptr, *span_ends = nullptr;
+    AttnItem *items = nullptr;
+    float *pooled = nullptr;
+    float *x = nullptr;
+    __nv_bfloat16 *xb = nullptr, *xb_lo = nullptr;
+    void *qkv = nullptr;
+    __nv_bfloat16 *att = nullptr, *att_lo = nullptr, *hmid = nullptr, *hmid_lo = nullptr;
+    // pinned host staging
+    int *h_ids = nullptr, *h_offsets = nullptr, *h_err = nullptr, *h_spans = nullptr;
+    AttnItem *h_items = nullptr;
+    float *h_out = nullptr;
+};
+
+struct Device {
+    int dev = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    void *embed = nullptr;
+    int embed_bf16 = 0;
+    float *pos_table = nullptr, *type0 = nullptr, *emb_ln_g = nullptr, *emb_ln_b = nullptr;
+    float *final_norm = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    int rope_cap = 0;
+    std::vector<LayerW> layers;
+    Workspace ws;
+    std::vector<void *> allocs;
+};
+
+}  // namespace
+}  // namespace fb
+
+struct ffwd_b200_ctx {
+    ffwd_config_t cfg;
+    int prec = 0;  // 0 bf16, 2 split 2-pass, 3 split 3-pass
+    std::vector<fb::Device> devs;
+    float lin_flops_per_token = 0.0f;
+};
+
+namespace fb {
+namespace {
+
+// ------------------------------------------------------------------ uploads
+
+template <typename T>
+int dev_alloc(Device &D, T **p, size_t count) {
+    void *q = nullptr;
+    CK(cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T)));
+    D.allocs.push_back(q);
+    *p = static_cast<T *>(q);
+    return 0;
+}
+
+template <typename T>
+int upload(Device &D, T **p, const std::vector<T> &h) {
+    if (dev_alloc(D, p, h.size())) return -1;
+    CK(cudaMemcpy(*p, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice));
+    return 0;
+}
+
+// Host copy of one (possibly fused) projection in its device encoding.
+struct HostMat {
+    std::vector<uint16_t> hi, lo;
+    int rows = 0, cols = 0;
+};
+
+// parts: row blocks concatenated in order (e.g. Wq, Wk, Wv).  interleave > 0
+// reorders two equal parts [G; U] as G0 U0 G1 U1 ... in blocks of `interleave`
+// rows, so one BN-wide GEMM tile holds matching gate and up columns.
+bool prep_mat(const std::vector<const TensorView *> &parts, const std::vector<std::string> &names,
+              int cols, bool split, int interleave, HostMat &hm, std::string &err) {
+    int rows = 0;
+    for (size_t i = 0; i < parts.size(); ++i) {
+        const TensorView *t = parts[i];
+        if (!t || t->shape.size() != 2 || t->shape[1] != cols) {
+            err = "missing or mis-shaped tensor " + names[i];
+            return false;
+        }
+        rows += (int)t->shape[0];
+    }
+    hm.rows = rows;
+    hm.cols = cols;
+    hm.hi.resize((size_t)rows * cols);
+    if (split) hm.lo.assign((size_t)rows * cols, 0);
+    std::vector<int> src_part(rows), src_row(rows);
+    {
+        int r = 0;
+        if (interleave > 0) {
+            const int half = (int)parts[0]->shape[0];
+            for (int blk = 0; blk < half / interleave; ++blk)
+                for (int p = 0; p < 2; ++p)
+                    for (int i = 0; i < interleave; ++i, ++r) {
+                        src_part[r] = p;
+                        src_row[r] = blk * interleave + i;
+                    }
+        } else {
+            for (size_t p = 0; p < parts.size(); ++p)
+                for (int i = 0; i < (int)parts[p]->shape[0]; ++i, ++r) {
+                    src_part[r] = (int)p;
+                    src_row[r] = i;
+                }
+        }
+    }
+    auto work = [&](int r0, int r1) {
+        for (int r = r0; r < r1; ++r) {
+            const TensorView *t = parts[src_part[r]];
+            const size_t so = (size_t)src_row[r] * cols;
+            uint16_t *dh = hm.hi.data() + (size_t)r * cols;
+            uint16_t *dl = split ? hm.lo.data() + (size_t)r * cols : nullptr;
+            if (t->dtype == DType::BF16) {
+                memcpy(dh, (const uint16_t *)t->data + so, (size_t)cols * 2);
+            } else {
+                for (int c = 0; c < cols; ++c) {
+                    float v = t->dtype == DType::F32 ? ((const float *)t->data)[so + c]
+                                                     : f16_to_f32(((const uint16_t *)t->data)[so + c]);
+                    uint16_t h = f32_to_bf16_rne(v);
+                    dh[c] = h;
+                    if (dl) dl[c] = f32_to_bf16_rne(v - bf16_to_f32(h));
+                }
+            }
+        }
+    };
+    const int nth = std::max(1, std::min(16, (int)std::thread::hardware_concurrency()));
+    std::vector<std::thread> th;
+    const int per = (rows + nth - 1) / nth;
+    for (int i = 0; i < nth; ++i) {
+        int a = i * per, b = std::min(rows, a + per);
+        if (a < b) th.emplace_back(work, a, b);
+    }
+    for (auto &t : th) t.join();
+    return true;
+}
+
+int upload_mat(Device &D, const HostMat &hm, int bn, Mat &m) {
+    m.rows = hm.rows;
+    m.cols = hm.cols;
+    m.bn = bn;
+    if (dev_alloc(D, &m.hi, hm.hi.size())) return -1;
+    CK(cudaMemcpy(m.hi, hm.hi.data(), hm.hi.size() * 2, cudaMemcpyHostToDevice));
+    if (make_map(&m.map_hi, m.hi, m.rows, m.cols, bn, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
+    if (!hm.lo.empty()) {
+        if (dev_alloc(D, &m.lo, hm.lo.size())) return -1;
+        CK(cudaMemcpy(m.lo, hm.lo.data(), hm.lo.size() * 2, cudaMemcpyHostToDevice));
+        if (make_map(&m.map_lo, m.lo, m.rows, m.cols, bn, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
+    }
+    return 0;
+}
+
+int pick_bn(int n) { return n % 256 == 0 ? 256 : 128; }
+
+// RoPE cos/sin cache exactly as libffwd/model_blas.c:85-123 computes it
+// (f32 powf / cosf / sinf), keeping the first half (the halves are equal).
+int ensure_rope(Device &D, const ffwd_config_t &c, int n_pos) {
+    if (n_pos <= D.rope_cap) return 0;
+    int cap = D.rope_cap > 0 ? D.rope_cap : 4096;
+    while (cap < n_pos) cap *= 2;
+    const int half = c.head_dim / 2;
+    std::vector<float> hc((size_t)cap * half), hs((size_t)cap * half);
+    for (int p = 0; p < cap; ++p) {
+        const float fp = (float)p;
+        for (int d = 0; d < half; ++d) {
+            const float inv = 1.0f / powf(c.rope_theta, (float)(2 * d) / (float)c.head_dim);
+            const float a = fp * inv;
+            hc[(size_t)p * half + d] = cosf(a);
+            hs[(size_t)p * half + d] = sinf(a);
+        }
+    }
+    CK(cudaSetDevice(D.dev));
+    CK(cudaStreamSynchronize(D.stream));
+    if (D.rope_cos) CK(cudaFree(D.rope_cos));
+    if (D.rope_sin) CK(cudaFree(D.rope_sin));
+    CK(cudaMalloc(&D.rope_cos, hc.size() * 4));
+    CK(cudaMalloc(&D.rope_sin, hs.size() * 4));
+    CK(cudaMemcpy(D.rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(D.rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice));
+    D.rope_cap = cap;
+    return 0;
+}
+
+// ------------------------------------------------------------------ load
+
+struct HostModel {
+    ffwd_config_t cfg;
+    int prec = 0;
+    std::string prefix;
+    SafeTensors st;
+};
+
+int load_device(HostModel &hm, Device &D, std::string &err) {
+    const ffwd_config_t &c = hm.cfg;
+    CK(cudaSetDevice(D.dev));
+    CK(cudaStreamCreateWithFlags(&D.stream, cudaStreamNonBlocking));
+    CK(cudaDeviceGetAttribute(&D.num_sms, cudaDevAttrMultiProcessorCount, D.dev));
+    const bool split_w = hm.prec == 3;
+    const int H = c.hidden_size, I = c.intermediate_size;
+    const std::string &p = hm.prefix;
+    auto T = [&](const std::string &n) { return hm.st.find(n); };
+    auto vec = [&](const std::string &n, std::vector<int64_t> shape, float **dst) -> int {
+        std::vector<float> h;
+        if (!tensor_to_f32(T(n), shape, h, err, n)) return -1;
+        return upload(D, dst, h);
+    };
+    auto mat = [&](std::vector<std::string> names, int cols, int interleave, int bn, Mat &m) -> int {
+        std::vector<const TensorView *> parts;
+        for (auto &n : names) parts.push_back(T(n));
+        HostMat h;
+        if (!prep_mat(parts, names, cols, split_w, interleave, h, err)) return -1;
+        return upload_mat(D, h, bn, m);
+    };
+
+    // Embedding table: kept in the file dtype (it is only gathered).
+    const std::string emb_name = c.family == FFWD_FAMILY_BERT ? p + "embeddings.word_embeddings.weight"
+                                                              : p + "embed_tokens.weight";
+    const TensorView *emb = T(emb_name);
+    if (!emb || emb->shape != std::vector<int64_t>{c.vocab_size, H}) {
+        err = "missing or mis-shaped " + emb_name;
+        return -1;
+    }
+    if (emb->dtype == DType::BF16) {
+        D.embed_bf16 = 1;
+        void *q;
+        CK(cudaMalloc(&q, emb->nbytes));
+        D.allocs.push_back(q);
+        CK(cudaMemcpy(q, emb->data, emb->nbytes, cudaMemcpyHostToDevice));
+        D.embed = q;
+    } else {
+        std::vector<float> h;
+        if (!tensor_to_f32(emb, {c.vocab_size, H}, h, err, emb_name)) return -1;
+        float *q;
+        if (upload(D, &q, h)) return -1;
+        D.embed = q;
+        D.embed_bf16 = 0;
+    }
+
+    D.layers.resize(c.n_layers);
+    if (c.family == FFWD_FAMILY_BERT) {
+        if (vec(p + "embeddings.position_embeddings.weight", {c.max_position_embeddings, H},
+                &D.pos_table) ||
+            vec(p + "embeddings.LayerNorm.weight", {H}, &D.emb_ln_g) ||
+            vec(p + "embeddings.LayerNorm.bias", {H}, &D.emb_ln_b))
+            return -1;
+        {
+            std::vector<float> h;
+            const std::string n = p + "embeddings.token_type_embeddings.weight";
+            if (!tensor_to_f32(T(n), {c.type_vocab_size, H}, h, err, n)) return -1;
+            h.resize(H);  // token type 0
+            if (upload(D, &D.type0, h)) return -1;
+        }
+        for (int i = 0; i < c.n_layers; ++i) {
+            LayerW &l = D.layers[i];
+            const std::string lp = p + "encoder.layer." + std::to_string(i) + ".";
+            if (mat({lp + "attention.self.query.weight", lp + "attention.self.key.weight",
+                     lp + "attention.self.value.weight"},
+                    H, 0, pick_bn(3 * H), l.qkv) ||
+                mat({lp + "attention.output.dense.weight"}, H, 0, pick_bn(H), l.o) ||
+                mat({lp + "intermediate.dense.weight"}, H, 0, pick_bn(I), l.up) ||
+                mat({lp + "output.dense.weight"}, I, 0, pick_bn(H), l.down))
+                return -1;
+            std::vector<float> bq, bk, bv;
+            if (!tensor_to_f32(T(lp + "attention.self.query.bias"), {H}, bq, err, "query.bias") ||
+                !tensor_to_f32(T(lp + "attention.self.key.bias"), {H}, bk, err, "key.bias") ||
+                !tensor_to_f32(T(lp + "attention.self.value.bias"), {H}, bv, err, "value.bias"))
+                return -1;
+            bq.insert(bq.end(), bk.begin(), bk.end());
+            bq.insert(bq.end(), bv.begin(), bv.end());
+            if (upload(D, &l.b_qkv, bq)) return -1;
+            if (vec(lp + "attention.output.dense.bias", {H}, &l.b_o) ||
+                vec(lp + "attention.output.LayerNorm.weight", {H}, &l.ln1_g) ||
+                vec(lp + "attention.output.LayerNorm.bias", {H}, &l.ln1_b) ||
+                vec(lp + "intermediate.dense.bias", {I}, &l.b_up) ||
+                vec(lp + "output.dense.bias", {H}, &l.b_down) ||
+                vec(lp + "output.LayerNorm.weight", {H}, &l.ln2_g) ||
+                vec(lp + "output.LayerNorm.bias", {H}, &l.ln2_b))
+                return -1;
+        }
+    } else {
+        const int qkv_out = c.q_dim + 2 * c.kv_dim;
+        for (int i = 0; i < c.n_layers; ++i) {
+            LayerW &l = D.layers[i];
+            const std::string lp = p + "layers." + std::to_string(i) + ".";
+            const int gu_bn = (I % 128 == 0) ? 256 : 128;
+            l.swiglu_half = gu_bn / 2;
+            if (mat({lp + "self_attn.q_proj.weight", lp + "self_attn.k_proj.weight",
+                     lp + "self_attn.v_proj.weight"},
+                    H, 0, qkv_out % 256 == 0 && 256 % c.head_dim == 0 ? 256 : 128, l.qkv) ||
+                mat({lp + "self_attn.o_proj.weight"}, c.q_dim, 0, pick_bn(H), l.o) ||
+                mat({lp + "mlp.gate_proj.weight", lp + "mlp.up_proj.weight"}, H, l.swiglu_half,
+                    gu_bn, l.up) ||
+                mat({lp + "mlp.down_proj.weight"}, I, 0, pick_bn(H), l.down))
+                return -1;
+            if (c.qkv_bias) {
+                std::vector<float> bq, bk, bv;
+                if (!tensor_to_f32(T(lp + "self_attn.q_proj.bias"), {c.q_dim}, bq, err, "q_proj.bias") ||
+                    !tensor_to_f32(T(lp + "self_attn.k_proj.bias"), {c.kv_dim}, bk, err, "k_proj.bias") ||
+                    !tensor_to_f32(T(lp + "self_attn.v_proj.bias"), {c.kv_dim}, bv, err, "v_proj.bias"))
+                    return -1;
+                bq.insert(bq.end(), bk.begin(), bk.end());
+                bq.insert(bq.end(), bv.begin(), bv.end());
+                if (upload(D, &l.b_qkv, bq)) return -1;
+            }
+            if (c.qk_norm && (vec(lp + "self_attn.q_norm.weight", {c.head_dim}, &l.q_norm) ||
+                              vec(lp + "self_attn.k_norm.weight", {c.head_dim}, &l.k_norm)))
+                return -1;
+            if (vec(lp + "input_layernorm.weight", {H}, &l.in_norm) ||
+                vec(lp + "post_attention_layernorm.weight", {H}, &l.post_norm))
+                return -1;
+        }
+        if (vec(p + "norm.weight", {H}, &D.final_norm)) return -1;
+        if (ensure_rope(D, c, 4096)) return -1;
+    }
+    return 0;
+}
+
+void free_device(Device &D) {
+    cudaSetDevice(D.dev);
+    if (D.stream) cudaStreamSynchronize(D.stream);
+    for (void *q : D.allocs) cudaFree(q);
+    D.allocs.clear();
+    Workspace &w = D.ws;
+    void *dptrs[] = {w.ids, w.pos, w.offsets, w.err, w.span_starts, w.span_ends, w.items, w.pooled,
+                     w.x, w.xb, w.xb_lo, w.qkv, w.att, w.att_lo, w.hmid, w.hmid_lo, D.rope_cos,
+                     D.rope_sin};
+    for (void *q : dptrs)
+        if (q) cudaFree(q);
+    void *hptrs[] = {w.h_ids, w.h_offsets, w.h_err, w.h_items, w.h_out, w.h_spans};
+    for (void *q : hptrs)
+        if (q) cudaFreeHost(q);
+    if (D.stream) cudaStreamDestroy(D.stream);
+    D = Device();
+}
+
+// ------------------------------------------------------------------ workspace
+
+int ensure_ws(ffwd_b200_ctx *ctx, Device &D, int T, int B, int n_items, int n_spans) {
+    Workspace &w = D.ws;
+    const ffwd_config_t &c = ctx->cfg;
+    const bool split = ctx->prec != 0;
+    if (T > w.cap_t) {
+        CK(cudaStreamSynchronize(D.stream));
+        const int cap = std::max(T, std::min(g_max_tokens, std::max(T, 2 * w.cap_t)));
+        void **bufs[] = {(void **)&w.ids, (void **)&w.pos, (void **)&w.x, (void **)&w.xb,
+                         (void **)&w.xb_lo, &w.qkv, (void **)&w.att, (void **)&w.att_lo,
+                         (void **)&w.hmid, (void **)&w.hmid_lo};
+        for (void **b : bufs)
+            if (*b) {
+                CK(cudaFree(*b));
+                *b = nullptr;
+            }
+        if (w.h_ids) CK(cudaFreeHost(w.h_ids));
+        const size_t t = (size_t)cap;
+        const int H = c.hidden_size, qkv = c.q_dim + 2 * c.kv_dim;
+        const int inter = c.intermediate_size;
+        CK(cudaMalloc(&w.ids, t * 4));
+        CK(cudaMalloc(&w.pos, t * 4));
+        CK(cudaMalloc(&w.x, t * H * 4));
+        CK(cudaMalloc(&w.xb, t * H * 2));
+        CK(cudaMalloc(&w.qkv, t * qkv * (split ? 4 : 2)));
+        CK(cudaMalloc(&w.att, t * c.q_dim * 2));
+        CK(cudaMalloc(&w.hmid, t * inter * 2));
+        if (split) {
+            CK(cudaMalloc(&w.xb_lo, t * H * 2));
+            CK(cudaMalloc(&w.att_lo, t * c.q_dim * 2));
+            CK(cudaMalloc(&w.hmid_lo, t * inter * 2));
+        }
+        CK(cudaMallocHost(&w.h_ids, t * 4));
+        w.cap_t = cap;
+    }
+    if (B + 1 > w.cap_b) {
+        CK(cudaStreamSynchronize(D.stream));
+        const int cap = std::max(B + 1, 2 * w.cap_b);
+        if (w.offsets) CK(cudaFree(w.offsets));
+        if (w.pooled) CK(cudaFree(w.pooled));
+        if (w.h_offsets) CK(cudaFreeHost(w.h_offsets));
+        if (w.h_out) CK(cudaFreeHost(w.h_out));
+        CK(cudaMalloc(&w.offsets, (size_t)cap * 4));
+        CK(cudaMalloc(&w.pooled, (size_t)cap * c.hidden_size * 4));
+        CK(cudaMallocHost(&w.h_offsets, (size_t)cap * 4));
+        CK(cudaMallocHost(&w.h_out, (size_t)cap * c.hidden_size * 4));
+        w.cap_b = cap;
+    }
+    if (n_items > w.cap_items) {
+        CK(cudaStreamSynchronize(D.stream));
+        const int cap = std::max(n_items, 2 * w.cap_items);
+        if (w.items) CK(cudaFree(w.items));
+        if (w.h_items) CK(cudaFreeHost(w.h_items));
+        CK(cudaMalloc(&w.items, (size_t)cap * sizeof(AttnItem)));
+        CK(cudaMallocHost(&w.h_items, (size_t)cap * sizeof(AttnItem)));
+        w.cap_items = cap;
+    }
+    if (n_spans > w.cap_spans) {
+        CK(cudaStreamSynchronize(D.stream));
+        const int cap = std::max(n_spans, 2 * w.cap_spans);
+        if (w.span_starts) CK(cudaFree(w.span_starts));
+        if (w.span_ends) CK(cudaFree(w.span_ends));
+        if (w.h_spans) CK(cudaFreeHost(w.h_spans));
+        CK(cudaMalloc(&w.span_starts, (size_t)cap * 4));
+        CK(cudaMalloc(&w.span_ends, (size_t)cap * 4));
+        CK(cudaMallocHost(&w.h_spans, (size_t)cap * 2 * 4));
+        if (w.pooled && n_spans + 1 > w.cap_b) {
+            CK(cudaFree(w.pooled));
+            CK(cudaFreeHost(w.h_out));
+            CK(cudaMalloc(&w.pooled, (size_t)cap * c.hidden_size * 4));
+            CK(cudaMallocHost(&w.h_out, (size_t)cap * c.hidden_size * 4));
+            w.cap_b = cap;
+        }
+        w.cap_spans = cap;
+    }
+    if (!w.err) {
+        CK(cudaMalloc(&w.err, 4));
+        CK(cudaMallocHost(&w.h_err, 4));
+    }
+    return 0;
+}
+
+// ------------------------------------------------------------------ forward
+
+__global__ void positions_kernel(const int *offsets, int pos_offset, int *pos) {
+    const int b = blockIdx.x;
+    const int s = offsets[b], e = offsets[b + 1];
+    for (int t = s + threadIdx.x; t < e; t += blockDim.x) pos[t] = pos_offset + (t - s);
+}
+
+int gemm(Device &D, int prec, const CUtensorMap *a, const CUtensorMap *a_lo, const Mat &w,
+         GemmParams &p) {
+    p.N = w.rows;
+    p.K = w.cols;
+    const int passes = prec == 0 ? 1 : prec;
+    LAUNCH(gemm_launch(a, passes >= 2 ? a_lo : nullptr, &w.map_hi, passes == 3 ? &w.map_lo : nullptr,
+                       w.bn, passes, p, D.num_sms, D.stream));
+    return 0;
+}
+
+// The forward over the packed rows already uploaded to D.ws (ids, offsets on
+// device; h_offsets on host).  Leaves final hidden states in ws.x.
+int forward(ffwd_b200_ctx *ctx, Device &D, int T, int B, const int *h_offsets) {
+    const ffwd_config_t &c = ctx->cfg;
+    Workspace &w = D.ws;
+    const int prec = ctx->prec;
+    const bool split = prec != 0;
+    const int H = c.hidden_size, I = c.intermediate_size;
+    const int qkv_dim = c.q_dim + 2 * c.kv_dim;
+    const bool bert = c.family == FFWD_FAMILY_BERT;
+    const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
+    cudaStream_t s = D.stream;
+
+    int max_len = 0;
+    for (int b = 0; b < B; ++b) max_len = std::max(max_len, h_offsets[b + 1] - h_offsets[b]);
+    if (!bert && ensure_rope(D, c, max_len)) return -1;
+
+    // Attention work list, heaviest first.
+    const int qt = split ? attention_f32_qtile(c.head_dim) : 128;
+    int n_items = 0;
+    {
+        std::vector<std::pair<int, AttnItem>> items;
+        for (int b = 0; b < B; ++b) {
+            const int L = h_offsets[b + 1] - h_offsets[b];
+            const int nq = (L + qt - 1) / qt;
+            for (int t = 0; t < nq; ++t) {
+                const int cost = c.attention_mode == FFWD_ATTENTION_CAUSAL ? t + 1 : nq;
+                items.push_back({cost, AttnItem{b, t}});
+            }
+        }
+        std::stable_sort(items.begin(), items.end(),
+                         [](const std::pair<int, AttnItem> &x, const std::pair<int, AttnItem> &y) {
+                             return x.first > y.first;
+                         });
+        if (ensure_ws(ctx, D, T, B, (int)items.size(), 0)) return -1;
+        for (size_t i = 0; i < items.size(); ++i) w.h_items[i] = items[i].second;
+        CK(cudaMemcpyAsync(w.items, w.h_items, items.size() * sizeof(AttnItem),
+                           cudaMemcpyHostToDevice, s));
+        n_items = (int)items.size();
+    }
+
+    // Activation tensor maps for this T.
+    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv;
+    if (make_map(&m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&m_att, w.att, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&m_h, w.hmid, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    if (split && (make_map(&m_xb_lo, w.xb_lo, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  make_map(&m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  make_map(&m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return -1;
+    if (!split && make_map(&m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
+                           c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
+
+    LAUNCH((positions_kernel<<<B, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0, w.pos),
+            cudaGetLastError()));
+    if (bert)
+        LAUNCH(embed_ln_launch(w.ids, w.pos, T, D.embed, D.embed_bf16, c.vocab_size, D.pos_table,
+                               D.type0, D.emb_ln_g, D.emb_ln_b, H, eps, w.x, xb_out, w.err, s));
+    else
+        LAUNCH(embed_rms_launch(w.ids, T, D.embed, D.embed_bf16, c.vocab_size, H, w.x,
+                                D.layers[0].in_norm, eps, xb_out, w.err, s));
+
+    AttnParams ap{};
+    ap.offsets = w.offsets;
+    ap.items = w.items;
+    ap.n_items = n_items;
+    ap.n_heads = c.n_heads;
+    ap.n_kv_heads = c.n_kv_heads;
+    ap.head_dim = c.head_dim;
+    ap.q_col0 = 0;
+    ap.k_col0 = c.q_dim;
+    ap.v_col0 = c.q_dim + c.kv_dim;
+    ap.causal = c.attention_mode == FFWD_ATTENTION_CAUSAL;
+    ap.scale = 1.0f / sqrtf((float)c.head_dim);
+    ap.out = w.att;
+    ap.ldo = c.q_dim;
+    ap.qkv_f32 = static_cast<const float *>(w.qkv);
+    ap.ldq = qkv_dim;
+    ap.out_hi = w.att;
+    ap.out_lo = w.att_lo;
+    ap.err = w.err;
+
+    for (int li = 0; li < c.n_layers; ++li) {
+        const LayerW &l = D.layers[li];
+        // ---- QKV projection (+ bias, + QK-norm and RoPE on the decoder)
+        {
+            GemmParams p{};
+            p.M = T;
+            p.out = w.qkv;
+            p.ldo = qkv_dim;
+            p.out_mode = split ? kOutF32 : kOutBF16;
+            p.bias = l.b_qkv;
+            p.err = w.err;
+            if (bert) {
+                p.epi = kEpiStore;
+            } else {
+                p.epi = kEpiQKRope;
+                p.pos = w.pos;
+                p.rope_cos = D.rope_cos;
+                p.rope_sin = D.rope_sin;
+                p.q_norm = l.q_norm;
+                p.k_norm = l.k_norm;
+                p.n_q_heads = c.n_heads;
+                p.n_kv_heads = c.n_kv_heads;
+                p.head_dim = c.head_dim;
+                p.eps = c.rms_norm_eps;
+            }
+            if (gemm(D, prec, &m_xb, &m_xb_lo, l.qkv, p)) return -1;
+        }
+        // ---- attention
+        if (split)
+            LAUNCH(attention_f32_launch(ap, s));
+        else
+            LAUNCH(attention_tc_launch(&m_qkv, ap, s));
+        // ---- output projection + residual (+ bias)
+        {
+            GemmParams p{};
+            p.M = T;
+            p.epi = kEpiResid;
+            p.resid = w.x;
+            p.ldr = H;
+            p.bias = l.b_o;
+            p.err = w.err;
+            if (gemm(D, prec, &m_att, &m_att_lo, l.o, p)) return -1;
+        }
+        if (bert)
+            LAUNCH(layernorm_launch(w.x, T, H, l.ln1_g, l.ln1_b, eps, xb_out, s));
+        else
+            LAUNCH(rmsnorm_launch(w.x, T, H, l.post_norm, eps, xb_out, s));
+        // ---- FFN up (GELU) or gate/up (SwiGLU)
+        {
+            GemmParams p{};
+            p.M = T;
+            p.out = w.hmid;
+            p.out_lo = w.hmid_lo;
+            p.ldo = I;
+            p.out_mode = split ? kOutSplit : kOutBF16;
+            p.err = w.err;
+            if (bert) {
+                p.epi = kEpiGelu;
+                p.bias = l.b_up;
+                p.gelu_tanh = c.ffn_act == FFWD_ACT_GELU_TANH;
+            } else {
+                p.epi = kEpiSwiGLU;
+            }
+            if (gemm(D, prec, &m_xb, &m_xb_lo, l.up, p)) return -1;
+        }
+        // ---- FFN down + residual (+ bias)
+        {
+            GemmParams p{};
+            p.M = T;
+            p.epi = kEpiResid;
+            p.resid = w.x;
+            p.ldr = H;
+            p.bias = l.b_down;
+            p.err = w.err;
+            if (gemm(D, prec, &m_h, &m_h_lo, l.down, p)) return -1;
+        }
+        if (bert)
+            LAUNCH(layernorm_launch(w.x, T, H, l.ln2_g, l.ln2_b, eps, xb_out, s));
+        else if (li + 1 < c.n_layers)
+            LAUNCH(rmsnorm_launch(w.x, T, H, D.layers[li + 1].in_norm, eps, xb_out, s));
+    }
+    return 0;
+}
+
+int check_err(Device &D) {
+    if (D.ws.h_err[0] != 0) {
+        const int e = D.ws.h_err[0];
+        fail("device error %d (%s)", e,
+             e == kErrBadTokenId ? "invalid token id"
+             : e == kErrBadNorm  ? "zero or non-finite embedding norm"
+             : e == kErrWaitTimeout ? "device wait timed out"
+                                    : "unknown");
+        return -1;
+    }
+    return 0;
+}
+
+// Encode the sequences idx[] of inputs on device D (as one or more forwards of
+// at most g_max_tokens packed rows), writing pooled rows to out[idx[i]].
+int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
+                  const std::vector<int> &idx, float *out) {
+    const ffwd_config_t &c = ctx->cfg;
+    const int H = c.hidden_size;
+    CK(cudaSetDevice(D.dev));
+    size_t i0 = 0;
+    while (i0 < idx.size()) {
+        size_t i1 = i0;
+        long long tok = 0;
+        while (i1 < idx.size() && (i1 == i0 || tok + inputs[idx[i1]].n_tokens <= g_max_tokens)) {
+            tok += inputs[idx[i1]].n_tokens;
+            ++i1;
+        }
+        const int B = (int)(i1 - i0), T = (int)tok;
+        if (ensure_ws(ctx, D, T, B, 0, 0)) return -1;
+        Workspace &w = D.ws;
+        int off = 0;
+        for (int b = 0; b < B; ++b) {
+            const ffwd_input_t &in = inputs[idx[i0 + b]];
+            w.h_offsets[b] = off;
+            for (int t = 0; t < in.n_tokens; ++t) {
+                const int id = in.ids[t];
+                if (id < 0 || id >= c.vocab_size) {
+                    fail("invalid token id %d at input %d position %d", id, idx[i0 + b], t);
+                    return -1;
+                }
+            }
+            memcpy(w.h_ids + off, in.ids, (size_t)in.n_tokens * 4);
+            off += in.n_tokens;
+        }
+        w.h_offsets[B] = off;
+        CK(cudaMemcpyAsync(w.ids, w.h_ids, (size_t)T * 4, cudaMemcpyHostToDevice, D.stream));
+        CK(cudaMemcpyAsync(w.offsets, w.h_offsets, (size_t)(B + 1) * 4, cudaMemcpyHostToDevice,
+                           D.stream));
+        CK(cudaMemsetAsync(w.err, 0, 4, D.stream));
+        if (forward(ctx, D, T, B, w.h_offsets)) return -1;
+        LAUNCH(pool_launch(w.x, w.offsets, B, H, c.pooling_mode,
+                           c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm, c.rms_norm_eps,
+                           c.normalize_embeddings, w.pooled, w.err, D.stream));
+        CK(cudaMemcpyAsync(w.h_out, w.pooled, (size_t)B * H * 4, cudaMemcpyDeviceToHost, D.stream));
+        CK(cudaMemcpyAsync(w.h_err, w.err, 4, cudaMemcpyDeviceToHost, D.stream));
+        CK(cudaStreamSynchronize(D.stream));
+        if (check_err(D)) return -1;
+        for (int b = 0; b < B; ++b)
+            memcpy(out + (size_t)idx[i0 + b] * H, w.h_out + (size_t)b * H, (size_t)H * 4);
+        i0 = i1;
+    }
+    return 0;
+}
+
+double seq_cost(const ffwd_b200_ctx *ctx, int L) {
+    const ffwd_config_t &c = ctx->cfg;
+    const double attn = c.attention_mode == FFWD_ATTENTION_CAUSAL ? 2.0 * c.q_dim * (L + 1.0)
+                                                                  : 4.0 * c.q_dim * (double)L;
+    return (double)L * ((double)ctx->lin_flops_per_token + attn * c.n_layers);
+}
+
+int validate_inputs(const ffwd_b200_ctx *ctx, const ffwd_input_t *inputs, int batch) {
+    if (!ctx || !inputs || batch <= 0) {
+        fail("invalid arguments");
+        return -1;
+    }
+    long long total = 0;
+    for (int b = 0; b < batch; ++b) {
+        if (!inputs[b].ids || inputs[b].n_tokens <= 0) {
+            fail("input %d is empty", b);
+            return -1;
+        }
+        if (ctx->cfg.family == FFWD_FAMILY_BERT &&
+            inputs[b].n_tokens > ctx->cfg.max_position_embeddings - ctx->cfg.position_id_offset) {
+            fail("sequence length %d plus position offset %d exceeds max_position_embeddings %d",
+                 inputs[b].n_tokens, ctx->cfg.position_id_offset,
+                 ctx->cfg.max_position_embeddings);
+            return -1;
+        }
+        total += inputs[b].n_tokens;
+        if (total > INT32_MAX) {
+            fail("batch too large");
+            return -1;
+        }
+    }
+    return 0;
+}
+
+}  // namespace
+}  // namespace fb
+
+using namespace fb;
+
+// ====================================================================== C ABI
+
+extern "C" {
+
+FFWD_B200_API int ffwd_b200_set_fast_gemm(const char *mode) {
+    if (!mode) return -1;
+    if (!strcmp(mode, "f32")) g_gemm_mode = 0;
+    else if (!strcmp(mode, "tf32")) g_gemm_mode = 1;
+    else if (!strcmp(mode, "bf16")) g_gemm_mode = 2;
+    else if (!strcmp(mode, "16f")) g_gemm_mode = 3;
+    else return -1;
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_set_weights_bf16(int on) {
+    g_weight_override = on ? 1 : 0;
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_set_weights_f16(int on) {
+    g_weight_override = on ? 2 : 0;
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_set_devices(const int *devices, int n) {
+    if (n <= 0 || !devices) return -1;
+    g_devices.assign(devices, devices + n);
+    g_devices_set = true;
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_set_max_tokens(int max_tokens) {
+    if (max_tokens < 1) return -1;
+    g_max_tokens = max_tokens;
+    return 0;
+}
+
+FFWD_B200_API const char *ffwd_b200_last_error(void) { return t_err.c_str(); }
+
+FFWD_B200_API long long ffwd_b200_launch_count(void) { return g_launches.load(); }
+
+FFWD_B200_API ffwd_b200_ctx_t *ffwd_b200_load(const char *model_dir) {
+    t_err.clear();
+    if (!model_dir) return nullptr;
+    auto hm = std::make_unique<HostModel>();
+    std::string err;
+    if (!parse_model_config(model_dir, hm->cfg, err) || !hm->st.open(model_dir, err)) {
+        fail("load %s: %s", model_dir, err.c_str());
+        return nullptr;
+    }
+    const ffwd_config_t &c = hm->cfg;
+    if (c.family == FFWD_FAMILY_BERT) {
+        if (hm->st.has("embeddings.word_embeddings.weight")) hm->prefix = "";
+        else if (hm->st.has("bert.embeddings.word_embeddings.weight")) hm->prefix = "bert.";
+        else if (hm->st.has("roberta.embeddings.word_embeddings.weight")) hm->prefix = "roberta.";
+        else {
+            fail("BERT-family word embeddings not found");
+            return nullptr;
+        }
+    } else {
+        if (hm->st.has("embed_tokens.weight")) hm->prefix = "";
+        else if (hm->st.has("model.embed_tokens.weight")) hm->prefix = "model.";
+        else {
+            fail("neither embed_tokens.weight nor model.embed_tokens.weight was found");
+            return nullptr;
+        }
+    }
+    // Supported shapes of this backend.
+    if (c.hidden_size % 128 != 0) {
+        fail("hidden_size %d must be a multiple of 128", c.hidden_size);
+        return nullptr;
+    }
+    if (c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128) {
+        fail("head_dim %d unsupported (32, 64 or 128)", c.head_dim);
+        return nullptr;
+    }
+    if (c.intermediate_size % 128 != 0 || c.hidden_size > 4096) {
+        fail("intermediate_size must be a multiple of 128 and hidden_size <= 4096");
+        return nullptr;
+    }
+
+    // Precision plan (mirrors libffwd/cuda.cu:189-247, 4225-4237, 5010-5019):
+    // weight storage follows the override, else the file dtype; the decoder
+    // with 16-bit weights always runs 16-bit operands.
+    const std::string probe = c.family == FFWD_FAMILY_BERT
+                                  ? hm->prefix + "encoder.layer.0.attention.self.query.weight"
+                                  : hm->prefix + "layers.0.self_attn.q_proj.weight";
+    const TensorView *pt = hm->st.find(probe);
+    if (!pt) {
+        fail("tensor not found: %s", probe.c_str());
+        return nullptr;
+    }
+    const bool w16 = g_weight_override >= 1 ||
+                     (g_weight_override < 0 && (pt->dtype == DType::BF16 || pt->dtype == DType::F16));
+    const bool exact = g_gemm_mode <= 1;
+    int prec;
+    if (c.family != FFWD_FAMILY_BERT)
+        prec = w16 ? 0 : (exact ? 3 : 0);
+    else
+        prec = exact ? (w16 ? 2 : 3) : 0;
+    hm->prec = prec;
+
+    auto *ctx = new ffwd_b200_ctx();
+    ctx->cfg = c;
+    ctx->prec = prec;
+    const int qkv_out = c.q_dim + 2 * c.kv_dim;
+    ctx->lin_flops_per_token =
+        2.0f * c.n_layers *
+        ((float)c.hidden_size * qkv_out + (float)c.q_dim * c.hidden_size +
+         (c.family == FFWD_FAMILY_BERT ? 2.0f : 3.0f) * c.hidden_size * c.intermediate_size);
+
+    std::vector<int> devs = g_devices;
+    if (!g_devices_set) {
+        devs.clear();
+        if (const char *e = getenv("FFWD_B200_DEVICES")) {
+            std::string s(e);
+            size_t pos = 0;
+            while (pos < s.size()) {
+                size_t q = s.find(',', pos);
+                if (q == std::string::npos) q = s.size();
+                if (q > pos) devs.push_back(atoi(s.substr(pos, q - pos).c_str()));
+                pos = q + 1;
+            }
+        }
+        if (devs.empty()) devs.push_back(0);
+    }
+    ctx->devs.resize(devs.size());
+    for (size_t i = 0; i < devs.size(); ++i) {
+        ctx->devs[i].dev = devs[i];
+        if (load_device(*hm, ctx->devs[i], err)) {
+            if (!err.empty()) fail("load %s on device %d: %s", model_dir, devs[i], err.c_str());
+            ffwd_b200_free(ctx);
+            return nullptr;
+        }
+    }
+    return ctx;
+}
+
+FFWD_B200_API void ffwd_b200_free(ffwd_b200_ctx_t *ctx) {
+    if (!ctx) return;
+    for (auto &D : ctx->devs) free_device(D);
+    delete ctx;
+}
+
+FFWD_B200_API const ffwd_config_t *ffwd_b200_config(const ffwd_b200_ctx_t *ctx) {
+    return ctx ? &ctx->cfg : nullptr;
+}
+
+FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx) { return ctx ? ctx->prec : -1; }
+
+FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts, int *part) {
+    if (n < 0 || n_parts <= 0 || (n > 0 && (!cost || !part))) return -1;
+    std::vector<int> order(n);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+    std::vector<double> load(n_parts, 0.0);
+    for (int i : order) {
+        int best = 0;
+        for (int p = 1; p < n_parts; ++p)
+            if (load[p] < load[best]) best = p;
+        part[i] = best;
+        load[best] += cost[i];
+    }
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_encode_batch(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs,
+                                         int batch, float *out) {
+    t_err.clear();
+    if (!out || validate_inputs(ctx, inputs, batch)) {
+        if (!out) fail("null output");
+        return -1;
+    }
+    const int nd = (int)ctx->devs.size();
+    if (nd == 1) {
+        std::vector<int> idx(batch);
+        std::iota(idx.begin(), idx.end(), 0);
+        return run_on_device(ctx, ctx->devs[0], inputs, idx, out);
+    }
+    std::vector<double> cost(batch);
+    for (int b = 0; b < batch; ++b) cost[b] = seq_cost(ctx, inputs[b].n_tokens);
+    std::vector<int> part(batch);
+    ffwd_b200_lpt_partition(cost.data(), batch, nd, part.data());
+    std::vector<std::vector<int>> idx(nd);
+    for (int b = 0; b < batch; ++b) idx[part[b]].push_back(b);
+    std::vector<int> rc(nd, 0);
+    std::vector<std::string> errs(nd);
+    std::vector<std::thread> th;
+    for (int d = 0; d < nd; ++d) {
+        if (idx[d].empty()) continue;
+        th.emplace_back([&, d] {
+            rc[d] = run_on_device(ctx, ctx->devs[d], inputs, idx[d], out);
+            errs[d] = t_err;
+        });
+    }
+    for (auto &t : th) t.join();
+    for (int d = 0; d < nd; ++d)
+        if (rc[d] != 0) {
+            t_err = errs[d];
+            return -1;
+        }
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_encode_into(ffwd_b200_ctx_t *ctx, const int *ids, int n, float *out) {
+    ffwd_input_t in{ids, n};
+    return ffwd_b200_encode_batch(ctx, &in, 1, out);
+}
+
+FFWD_B200_API float *ffwd_b200_encode(ffwd_b200_ctx_t *ctx, const int *ids, int n) {
+    if (!ctx) return nullptr;
+    float *out = (float *)malloc((size_t)ctx->cfg.hidden_size * sizeof(float));
+    if (!out) return nullptr;
+    if (ffwd_b200_encode_into(ctx, ids, n, out) != 0) {
+        free(out);
+        return nullptr;
+    }
+    return out;
+}
+
+FFWD_B200_API int ffwd_b200_encode_spans_batch(ffwd_b200_ctx_t *ctx,
+                                               const ffwd_context_input_t *inputs, int batch,
+                                               float *out) {
+    t_err.clear();
+    if (!ctx || !inputs || batch <= 0 || !out) {
+        fail("invalid arguments");
+        return -1;
+    }
+    std::vector<ffwd_input_t> packed(batch);
+    int total_spans = 0;
+    for (int b = 0; b < batch; ++b) {
+        const ffwd_context_input_t &in = inputs[b];
+        if (!in.input.ids || in.input.n_tokens <= 0 || !in.spans || in.n_spans <= 0) {
+            fail("invalid span input %d", b);
+            return -1;
+        }
+        for (int s = 0; s < in.n_spans; ++s) {
+            const int st = in.spans[s].start, len = in.spans[s].n_tokens;
+            if (st < 0 || len <= 0 || st > in.input.n_tokens || len > in.input.n_tokens - st) {
+                fail("invalid span %d of input %d", s, b);
+                return -1;
+            }
+        }
+        packed[b] = in.input;
+        total_spans += in.n_spans;
+    }
+    if (validate_inputs(ctx, packed.data(), batch)) return -1;
+    const ffwd_config_t &c = ctx->cfg;
+    Device &D = ctx->devs[0];
+    CK(cudaSetDevice(D.dev));
+    long long T64 = 0;
+    for (auto &p : packed) T64 += p.n_tokens;
+    const int T = (int)T64, H = c.hidden_size;
+    if (ensure_ws(ctx, D, T, batch, 0, total_spans)) return -1;
+    Workspace &w = D.ws;
+    int off = 0, si = 0;
+    for (int b = 0; b < batch; ++b) {
+        const ffwd_input_t &in = packed[b];
+        for (int t = 0; t < in.n_tokens; ++t)
+            if (in.ids[t] < 0 || in.ids[t] >= c.vocab_size) {
+                fail("invalid token id %d at input %d position %d", in.ids[t], b, t);
+                return -1;
+            }
+        w.h_offsets[b] = off;
+        memcpy(w.h_ids + off, in.ids, (size_t)in.n_tokens * 4);
+        for (int s = 0; s < inputs[b].n_spans; ++s, ++si) {
+            w.h_spans[si] = off + inputs[b].spans[s].start;
+            w.h_spans[total_spans + si] = off + inputs[b].spans[s].start + inputs[b].spans[s].n_tokens;
+        }
+        off += in.n_tokens;
+    }
+    w.h_offsets[batch] = off;
+    CK(cudaMemcpyAsync(w.ids, w.h_ids, (size_t)T * 4, cudaMemcpyHostToDevice, D.stream));
+    CK(cudaMemcpyAsync(w.offsets, w.h_offsets, (size_t)(batch + 1) * 4, cudaMemcpyHostToDevice,
+                       D.stream));
+    CK(cudaMemcpyAsync(w.span_starts, w.h_spans, (size_t)total_spans * 4, cudaMemcpyHostToDevice,
+                       D.stream));
+    CK(cudaMemcpyAsync(w.span_ends, w.h_spans + total_spans, (size_t)total_spans * 4,
+                       cudaMemcpyHostToDevice, D.stream));
+    CK(cudaMemsetAsync(w.err, 0, 4, D.stream));
+    if (forward(ctx, D, T, batch, w.h_offsets)) return -1;
+    LAUNCH(span_pool_launch(w.x, w.span_starts, w.span_ends, total_spans, H,
+                            c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm, c.rms_norm_eps,
+                            w.pooled, D.stream));
+    CK(cudaMemcpyAsync(w.h_out, w.pooled, (size_t)total_spans * H * 4, cudaMemcpyDeviceToHost,
+                       D.stream));
+    CK(cudaMemcpyAsync(w.h_err, w.err, 4, cudaMemcpyDeviceToHost, D.stream));
+    CK(cudaStreamSynchronize(D.stream));
+    if (check_err(D)) return -1;
+    memcpy(out, w.h_out, (size_t)total_spans * H * 4);
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const int *d_ids,
+                                          const int *h_offsets, int batch, float *d_out, int sync) {
+    t_err.clear();
+    if (!ctx || dev < 0 || dev >= (int)ctx->devs.size() || !d_ids || !h_offsets || batch <= 0 ||
+        !d_out) {
+        fail("invalid arguments");
+        return -1;
+    }
+    const ffwd_config_t &c = ctx->cfg;
+    Device &D = ctx->devs[dev];
+    CK(cudaSetDevice(D.dev));
+    const int T = h_offsets[batch];
+    for (int b = 0; b < batch; ++b) {
+        const int L = h_offsets[b + 1] - h_offsets[b];
+        if (L <= 0 || (c.family == FFWD_FAMILY_BERT &&
+                       L > c.max_position_embeddings - c.position_id_offset)) {
+            fail("invalid sequence length %d at %d", L, b);
+            return -1;
+        }
+    }
+    if (ensure_ws(ctx, D, T, batch, 0, 0)) return -1;
+    Workspace &w = D.ws;
+    memcpy(w.h_offsets, h_offsets, (size_t)(batch + 1) * 4);
+    CK(cudaMemcpyAsync(w.ids, d_ids, (size_t)T * 4, cudaMemcpyDeviceToDevice, D.stream));
+    CK(cudaMemcpyAsync(w.offsets, w.h_offsets, (size_t)(batch + 1) * 4, cudaMemcpyHostToDevice,
+                       D.stream));
+    CK(cudaMemsetAsync(w.err, 0, 4, D.stream));
+    if (forward(ctx, D, T, batch, w.h_offsets)) return -1;
+    LAUNCH(pool_launch(w.x, w.offsets, batch, c.hidden_size, c.pooling_mode,
+                       c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm, c.rms_norm_eps,
+                       c.normalize_embeddings, d_out, w.err, D.stream));
+    if (sync) {
+        CK(cudaMemcpyAsync(w.h_err, w.err, 4, cudaMemcpyDeviceToHost, D.stream));
+        CK(cudaStreamSynchronize(D.stream));
+        if (check_err(D)) return -1;
+    }
+    return 0;
+}
+
+FFWD_B200_API void *ffwd_b200_stream(ffwd_b200_ctx_t *ctx, int dev) {
+    if (!ctx || dev < 0 || dev >= (int)ctx->devs.size()) return nullptr;
+    return ctx->devs[dev].stream;
+}
+
+FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const void *w,
+                                      const void *w_lo, float *y, int M, int N, int K, int bn) {
+    t_err.clear();
+    if (!x || !w || !y || M <= 0 || N <= 0 || K <= 0 || (bn != 128 && bn != 256)) {
+        fail("invalid arguments");
+        return -1;
+    }
+    int dev = 0, sms = 148;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CUtensorMap ma, mal, mb, mbl;
+    if (make_map(&ma, x, M, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&mb, w, N, K, bn, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    if (x_lo && make_map(&mal, x_lo, M, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
+    if (w_lo && make_map(&mbl, w_lo, N, K, bn, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
+    const int passes = x_lo ? (w_lo ? 3 : 2) : 1;
+    if (w_lo && !x_lo) {
+        fail("w_lo requires x_lo");
+        return -1;
+    }
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.epi = kEpiStore;
+    p.out_mode = kOutF32;
+    p.out = y;
+    p.ldo = N;
+    LAUNCH(gemm_launch(&ma, x_lo ? &mal : nullptr, &mb, w_lo ? &mbl : nullptr, bn, passes, p, sms,
+                       0));
+    CK(cudaDeviceSynchronize());
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,63 @@
+// Projection GEMM for the packed token matrix: Y[M, N] = X[M, K] * W[N, K]^T
+// on the sm_100a tensor cores (tcgen05.mma, accumulators in TMEM, operands
+// staged by TMA), with the layer's elementwise work fused into the epilogue.
+//
+// Replaces the reference's cuBLAS / cuBLASLt projections (libffwd/cuda.cu
+// linear_ex 2905-2969, linear_lt 3058-3182, linear_accum 3030-3038) and the
+// elementwise kernels that followed them (add_row_bias 402-407,
+// rms_norm_rope_qk 538-606, silu_mul_packed 611-624, bias_gelu* 2616-2708).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+namespace fb {
+
+// Epilogue kinds.
+enum GemmEpi : int {
+    kEpiStore = 0,   // out = acc (+ bias)
+    kEpiGelu = 1,    // out = gelu(acc + bias)            (erf or tanh curve)
+    kEpiResid = 2,   // resid[M, N] += acc (+ bias)       (f32, in place)
+    kEpiSwiGLU = 3,  // tile = [gate | up] halves -> out = silu(gate) * up
+    kEpiQKRope = 4,  // (+ bias) per-head RMSNorm (q/k heads) + NeoX RoPE
+};
+
+// Output encodings.
+enum OutMode : int {
+    kOutBF16 = 0,
+    kOutF32 = 1,
+    kOutSplit = 2,  // bf16 hi in `out`, bf16 lo (x - hi) in `out_lo`
+};
+
+struct GemmParams {
+    int M, N, K;
+    int epi;
+    int out_mode;
+    void *out;
+    void *out_lo;
+    int ldo;               // output row stride (elements)
+    float *resid;          // kEpiResid target [M, ldr]
+    int ldr;
+    const float *bias;     // [N] or null
+    int gelu_tanh;         // kEpiGelu curve
+    // kEpiQKRope
+    const int *pos;        // [M] position of each packed row
+    const float *rope_cos; // [n_pos, head_dim / 2]
+    const float *rope_sin;
+    const float *q_norm;   // [head_dim] or null (no QK-norm)
+    const float *k_norm;
+    int n_q_heads, n_kv_heads, head_dim;
+    float eps;
+    int *err;
+};
+
+// Host launcher.  Each tensor map is 2-D bf16 with a 64-column (128-byte) box
+// and 128-byte swizzle: A maps cover X (box rows 128), B maps cover W (box rows
+// BN).  `passes` = 1: A*B; 2: (A + A_lo)*B; 3: A*B + A*B_lo + A_lo*B.
+// Returns a cudaError_t value.
+int gemm_launch(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap *b,
+                const CUtensorMap *b_lo, int bn, int passes, const GemmParams &p, int num_sms,
+                cudaStream_t stream);
+
+}  // namespace fb

@@ -1,0 +1,347 @@
+// Row kernels (see rowops.cuh).  Rows are processed in 8-element groups
+// (one 16-byte bf16 load or two 16-byte f32 loads per lane); every pass of a
+// kernel uses the same lane -> column mapping, so a thread only re-reads what
+// it wrote itself.
+#include "rowops.cuh"
+#include "ptx.cuh"
+
+namespace fb {
+namespace {
+
+constexpr int kRowWarps = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ void load8_f32(const float *p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0];
+    const float4 b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void store8_f32(float *p, const float (&v)[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16 *p, float (&v)[8]) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+__device__ __forceinline__ void load8_ro_f32(const float *p, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void store8_out(RowOut o, size_t off, const float (&v)[8]) {
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * i]);
+        const __nv_bfloat16 h1 = __float2bfloat16_rn(v[2 * i + 1]);
+        __nv_bfloat162 hh(h0, h1);
+        hi[i] = *reinterpret_cast<uint32_t *>(&hh);
+        lo[i] = pack_bf16x2(v[2 * i] - __bfloat162float(h0), v[2 * i + 1] - __bfloat162float(h1));
+    }
+    *reinterpret_cast<uint4 *>(o.hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    if (o.lo) *reinterpret_cast<uint4 *>(o.lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+// ---------------------------------------------------------------- Qwen embed
+
+template <bool BF16>
+__global__ void __launch_bounds__(kRowWarps * 32)
+    embed_rms_kernel(const int *ids, int T, const void *table, int vocab, int H, float *x,
+                     const float *w, float eps, RowOut xn, int *err) {
+    const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= T) return;
+    int id = ids[row];
+    const bool bad = id < 0 || id >= vocab;
+    if (bad) {
+        if (lane == 0) set_error(err, kErrBadTokenId);
+        id = 0;
+    }
+    float *xr = x + (size_t)row * H;
+    float ss = 0.0f;
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8];
+        if (BF16)
+            load8_bf16(static_cast<const __nv_bfloat16 *>(table) + (size_t)id * H + c, v);
+        else
+            load8_ro_f32(static_cast<const float *>(table) + (size_t)id * H + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (bad) v[i] = 0.0f;
+            ss += v[i] * v[i];
+        }
+        store8_f32(xr + c, v);
+    }
+    if (!w) return;
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)H + eps);
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8], g[8];
+        load8_f32(xr + c, v);
+        load8_ro_f32(w + c, g);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
+        store8_out(xn, (size_t)row * H + c, v);
+    }
+}
+
+// ---------------------------------------------------------------- RMSNorm
+
+__global__ void __launch_bounds__(kRowWarps * 32)
+    rmsnorm_kernel(const float *x, int T, int H, const float *w, float eps, RowOut xn) {
+    const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= T) return;
+    const float *xr = x + (size_t)row * H;
+    float ss = 0.0f;
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8];
+        load8_f32(xr + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)H + eps);
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8], g[8];
+        load8_f32(xr + c, v);
+        load8_ro_f32(w + c, g);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
+        store8_out(xn, (size_t)row * H + c, v);
+    }
+}
+
+// ---------------------------------------------------------------- LayerNorm
+
+// Two-pass mean / variance as in libffwd/norm.c:107-138.
+__device__ __forceinline__ void layernorm_row(float *xr, int H, int lane, const float *g,
+                                              const float *b, float eps, RowOut xb, size_t off) {
+    float sum = 0.0f;
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8];
+        load8_f32(xr + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum += v[i];
+    }
+    const float inv_h = 1.0f / (float)H;
+    const float mean = warp_sum(sum) * inv_h;
+    float var = 0.0f;
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8];
+        load8_f32(xr + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float d = v[i] - mean;
+            var += d * d;
+        }
+    }
+    var = warp_sum(var) * inv_h;
+    const float inv_std = 1.0f / sqrtf(var + eps);
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8], gg[8], bb[8];
+        load8_f32(xr + c, v);
+        load8_ro_f32(g + c, gg);
+        load8_ro_f32(b + c, bb);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = gg[i] * (v[i] - mean) * inv_std + bb[i];
+        store8_f32(xr + c, v);
+        store8_out(xb, off + c, v);
+    }
+}
+
+__global__ void __launch_bounds__(kRowWarps * 32)
+    layernorm_kernel(float *x, int T, int H, const float *g, const float *b, float eps, RowOut xb) {
+    const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    if (row >= T) return;
+    layernorm_row(x + (size_t)row * H, H, threadIdx.x & 31, g, b, eps, xb, (size_t)row * H);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kRowWarps * 32)
+    embed_ln_kernel(const int *ids, const int *pos, int T, const void *table, int vocab,
+                    const float *pos_table, const float *type0, const float *g, const float *b,
+                    int H, float eps, float *x, RowOut xb, int *err) {
+    const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= T) return;
+    int id = ids[row];
+    const bool bad = id < 0 || id >= vocab;
+    if (bad) {
+        if (lane == 0) set_error(err, kErrBadTokenId);
+        id = 0;
+    }
+    const int ps = pos[row];
+    float *xr = x + (size_t)row * H;
+    for (int c = lane * 8; c < H; c += 256) {
+        float v[8], pv[8], tv[8];
+        if (BF16)
+            load8_bf16(static_cast<const __nv_bfloat16 *>(table) + (size_t)id * H + c, v);
+        else
+            load8_ro_f32(static_cast<const float *>(table) + (size_t)id * H + c, v);
+        load8_ro_f32(pos_table + (size_t)ps * H + c, pv);
+        load8_ro_f32(type0 + c, tv);
+        // Same association as libffwd/forward.c:362-365: (tok + pos) + type.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = bad ? 0.0f : (v[i] + pv[i]) + tv[i];
+        store8_f32(xr + c, v);
+    }
+    layernorm_row(xr, H, lane, g, b, eps, xb, (size_t)row * H);
+}
+
+// ---------------------------------------------------------------- pooling
+
+constexpr int kPoolThreads = 256;
+constexpr int kPoolMaxCols = 16;  // H <= 4096
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPoolThreads / 32; ++i) t += red[i];
+    return t;
+}
+
+// mode 0: mean over [start, end); 1: row end-1; 2: row start.
+__global__ void __launch_bounds__(kPoolThreads)
+    pool_kernel(const float *x, const int *starts, const int *ends, int H, int mode,
+                const float *norm_w, float eps, int normalize, float *out, int *err) {
+    __shared__ float red[kPoolThreads / 32];
+    const int b = blockIdx.x;
+    const int s = starts[b], e = ends[b];
+    float acc[kPoolMaxCols];
+#pragma unroll
+    for (int k = 0; k < kPoolMaxCols; ++k) acc[k] = 0.0f;
+
+    auto add_row = [&](int r) {
+        const float *xr = x + (size_t)r * H;
+        float v[kPoolMaxCols];
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kPoolMaxCols; ++k) {
+            const int d = threadIdx.x + k * kPoolThreads;
+            v[k] = d < H ? xr[d] : 0.0f;
+            ss += v[k] * v[k];
+        }
+        float inv = 1.0f;
+        if (norm_w) inv = 1.0f / sqrtf(block_sum(ss, red) / (float)H + eps);
+#pragma unroll
+        for (int k = 0; k < kPoolMaxCols; ++k) {
+            const int d = threadIdx.x + k * kPoolThreads;
+            if (d < H) acc[k] += norm_w ? v[k] * inv * norm_w[d] : v[k];
+        }
+    };
+
+    if (mode == 0) {
+        for (int r = s; r < e; ++r) add_row(r);
+        const float inv_len = 1.0f / (float)(e - s);
+#pragma unroll
+        for (int k = 0; k < kPoolMaxCols; ++k) acc[k] *= inv_len;
+    } else {
+        add_row(mode == 1 ? e - 1 : s);
+    }
+    if (normalize) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kPoolMaxCols; ++k) ss += acc[k] * acc[k];
+        ss = block_sum(ss, red);
+        if (!(ss > 0.0f) || !isfinite(ss)) {
+            if (threadIdx.x == 0) set_error(err, kErrBadNorm);
+            return;
+        }
+        const float inv = 1.0f / sqrtf(ss);
+#pragma unroll
+        for (int k = 0; k < kPoolMaxCols; ++k) acc[k] *= inv;
+    }
+#pragma unroll
+    for (int k = 0; k < kPoolMaxCols; ++k) {
+        const int d = threadIdx.x + k * kPoolThreads;
+        if (d < H) out[(size_t)b * H + d] = acc[k];
+    }
+}
+
+inline int row_blocks(int T) { return (T + kRowWarps - 1) / kRowWarps; }
+
+}  // namespace
+
+int embed_rms_launch(const int *ids, int T, const void *table, int table_bf16, int vocab, int H,
+                     float *x, const float *w, float eps, RowOut xn, int *err, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (table_bf16)
+        embed_rms_kernel<true><<<row_blocks(T), kRowWarps * 32, 0, s>>>(ids, T, table, vocab, H, x,
+                                                                       w, eps, xn, err);
+    else
+        embed_rms_kernel<false><<<row_blocks(T), kRowWarps * 32, 0, s>>>(ids, T, table, vocab, H, x,
+                                                                        w, eps, xn, err);
+    return cudaGetLastError();
+}
+
+int embed_ln_launch(const int *ids, const int *pos, int T, const void *table, int table_bf16,
+                    int vocab, const float *pos_table, const float *type0, const float *g,
+                    const float *b, int H, float eps, float *x, RowOut xb, int *err,
+                    cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (table_bf16)
+        embed_ln_kernel<true><<<row_blocks(T), kRowWarps * 32, 0, s>>>(
+            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err);
+    else
+        embed_ln_kernel<false><<<row_blocks(T), kRowWarps * 32, 0, s>>>(
+            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err);
+    return cudaGetLastError();
+}
+
+int rmsnorm_launch(const float *x, int T, int H, const float *w, float eps, RowOut xn,
+                   cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    rmsnorm_kernel<<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, w, eps, xn);
+    return cudaGetLastError();
+}
+
+int layernorm_launch(float *x, int T, int H, const float *g, const float *b, float eps,
+                     RowOut xb, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    layernorm_kernel<<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, g, b, eps, xb);
+    return cudaGetLastError();
+}
+
+int pool_launch(const float *x, const int *offsets, int batch, int H, int mode,
+                const float *norm_w, float eps, int normalize, float *out, int *err,
+                cudaStream_t s) {
+    if (batch <= 0) return cudaSuccess;
+    if (H > kPoolThreads * kPoolMaxCols) return cudaErrorInvalidValue;
+    pool_kernel<<<batch, kPoolThreads, 0, s>>>(x, offsets, offsets + 1, H, mode, norm_w, eps,
+                                                normalize, out, err);
+    return cudaGetLastError();
+}
+
+int span_pool_launch(const float *x, const int *starts, const int *ends, int n_spans, int H,
+                     const float *norm_w, float eps, float *out, cudaStream_t s) {
+    if (n_spans <= 0) return cudaSuccess;
+    if (H > kPoolThreads * kPoolMaxCols) return cudaErrorInvalidValue;
+    pool_kernel<<<n_spans, kPoolThreads, 0, s>>>(x, starts, ends, H, 0, norm_w, eps, 0, out,
+                                                  nullptr);
+    return cudaGetLastError();
+}
+
+}  // namespace fb

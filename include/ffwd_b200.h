@@ -1,0 +1,188 @@
+/*
+ * ffwd_b200 — B200 (sm_100a) backend for ffwd's packed, variable-length
+ * embedding forward pass.
+ *
+ * C ABI.  The first group mirrors the reference backend interface in
+ * libffwd/cuda.h one for one (ffwd_cuda_* -> ffwd_b200_*), so
+ * libffwd/backend_cuda.c can call these instead; the shared types are
+ * layout-identical copies of libffwd/ffwd.h so pointers pass straight through.
+ * The second group has no counterpart in the reference (multi-GPU device set,
+ * device-resident inputs, diagnostics).
+ *
+ * Conventions (as in the reference): 0 on success, -1 on failure, NULL on a
+ * failed load; diagnostics go to stderr and to ffwd_b200_last_error().  A
+ * context is used from one host thread at a time (the inference worker,
+ * libffwd/ffwd.h:118-128).
+ */
+#ifndef FFWD_B200_H
+#define FFWD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef FFWD_B200_API
+#    if defined(__GNUC__)
+#        define FFWD_B200_API __attribute__((visibility("default")))
+#    else
+#        define FFWD_B200_API
+#    endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- Shared types: identical layout to libffwd/ffwd.h:34-105 ------------- */
+#ifndef FFWD_H
+typedef enum {
+    FFWD_ATTENTION_BIDIRECTIONAL = 0,
+    FFWD_ATTENTION_CAUSAL = 1,
+} ffwd_attention_mode_t;
+
+typedef enum {
+    FFWD_POOL_MEAN = 0,
+    FFWD_POOL_LAST_TOKEN = 1,
+    FFWD_POOL_CLS = 2,
+} ffwd_pooling_mode_t;
+
+typedef enum {
+    FFWD_FAMILY_QWEN3 = 0,
+    FFWD_FAMILY_BERT = 1,
+} ffwd_family_t;
+
+typedef enum {
+    FFWD_ACT_GELU_ERF = 0,
+    FFWD_ACT_GELU_TANH = 1,
+} ffwd_act_t;
+
+typedef struct {
+    ffwd_family_t family;
+    ffwd_act_t ffn_act;
+    int hidden_size;
+    int n_layers;
+    int n_heads;
+    int n_kv_heads;
+    int head_dim;
+    int q_dim;
+    int kv_dim;
+    int intermediate_size;
+    int vocab_size;
+    int max_position_embeddings;
+    int position_id_offset;
+    int type_vocab_size;
+    float rms_norm_eps;
+    float layer_norm_eps;
+    float rope_theta;
+    int qk_norm;
+    int qkv_bias;
+    ffwd_attention_mode_t attention_mode;
+    ffwd_pooling_mode_t pooling_mode;
+    int normalize_embeddings;
+    int append_terminal_token;
+} ffwd_config_t;
+
+typedef struct {
+    const int *ids;
+    int n_tokens;
+} ffwd_input_t;
+
+typedef struct {
+    int start;
+    int n_tokens;
+} ffwd_span_t;
+
+typedef struct {
+    ffwd_input_t input;
+    const ffwd_span_t *spans;
+    int n_spans;
+} ffwd_context_input_t;
+#endif /* FFWD_H */
+
+typedef struct ffwd_b200_ctx ffwd_b200_ctx_t;
+
+/* ---- Mirror of libffwd/cuda.h ---------------------------------------------- */
+
+/* Process-wide GEMM mode, set before any load: "f32" | "tf32" | "bf16" | "16f".
+ * Replaces ffwd_cuda_set_fast_gemm (cuda.h:22; parsing at cuda.cu:169-199).
+ * f32 and tf32 run split-bf16 multi-pass GEMMs and f32 attention; bf16 and 16f
+ * run single-pass bf16 tensor-core GEMMs and attention. -1 on an unknown mode. */
+FFWD_B200_API int ffwd_b200_set_fast_gemm(const char *mode);
+/* Store weights as bf16 (on = 1) or in the file dtype (on = 0).
+ * Replaces ffwd_cuda_set_weights_bf16 (cuda.h:23; cuda.cu:237-247). */
+FFWD_B200_API int ffwd_b200_set_weights_bf16(int on);
+/* Replaces ffwd_cuda_set_weights_f16 (cuda.h:24).  16-bit weights are stored as
+ * bf16 on this backend. */
+FFWD_B200_API int ffwd_b200_set_weights_f16(int on);
+
+/* Load config + safetensors from model_dir and upload to every device of the
+ * current device set.  Replaces ffwd_cuda_load (cuda.h:26; cuda.cu:4306). */
+FFWD_B200_API ffwd_b200_ctx_t *ffwd_b200_load(const char *model_dir);
+/* Replaces ffwd_cuda_free (cuda.h:27). */
+FFWD_B200_API void ffwd_b200_free(ffwd_b200_ctx_t *ctx);
+/* Replaces ffwd_cuda_config (cuda.h:56). */
+FFWD_B200_API const ffwd_config_t *ffwd_b200_config(const ffwd_b200_ctx_t *ctx);
+
+/* One sequence -> out_embedding[hidden].  Replaces ffwd_cuda_encode_into
+ * (cuda.h:58-59). */
+FFWD_B200_API int ffwd_b200_encode_into(ffwd_b200_ctx_t *ctx, const int *token_ids, int n_tokens,
+                                        float *out_embedding);
+/* Malloc'd embedding or NULL.  Replaces ffwd_cuda_encode (cuda.h:60). */
+FFWD_B200_API float *ffwd_b200_encode(ffwd_b200_ctx_t *ctx, const int *token_ids, int n_tokens);
+/* Packed batch -> out_embeddings[batch * hidden] (host), input order.  Forward,
+ * pooling and L2 normalisation run on the device(s); sequences are sharded
+ * across the device set.  Replaces ffwd_cuda_encode_batch (cuda.h:61-64;
+ * cuda.cu:5102-5140). */
+FFWD_B200_API int ffwd_b200_encode_batch(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs,
+                                         int batch, float *out_embeddings);
+/* Contextual spans: one forward per batch, each span mean-pooled over the
+ * final hidden states, out[total_spans * hidden].  Replaces
+ * ffwd_cuda_encode_spans_batch (cuda.h:65-68; cuda.cu:5142-5225). */
+FFWD_B200_API int ffwd_b200_encode_spans_batch(ffwd_b200_ctx_t *ctx,
+                                               const ffwd_context_input_t *inputs, int batch,
+                                               float *out_embeddings);
+
+/* ---- No counterpart in the reference ------------------------------------ */
+
+/* Device set used by the next ffwd_b200_load (replicated weights, sequences
+ * sharded by LPT over estimated cost).  Default: $FFWD_B200_DEVICES
+ * ("0,1,..."), else device 0. */
+FFWD_B200_API int ffwd_b200_set_devices(const int *devices, int n_devices);
+
+/* Largest packed token count one device forward holds; longer batches run as
+ * several forwards (sequences are never split).  Default 65536. */
+FFWD_B200_API int ffwd_b200_set_max_tokens(int max_tokens);
+
+/* Device-resident entry (single device, index dev of the context's set): ids
+ * and out already in that GPU's memory, host row offsets [batch + 1].  Work is
+ * enqueued on the context's stream for that device; the call returns after
+ * the stream completes when sync != 0.  The bench's kernel-only timing uses
+ * this path. */
+FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const int *d_ids,
+                                          const int *h_offsets, int batch, float *d_out, int sync);
+
+/* The CUDA stream (cudaStream_t) the context uses on device index dev. */
+FFWD_B200_API void *ffwd_b200_stream(ffwd_b200_ctx_t *ctx, int dev);
+/* Kernel launches issued by this process since load (all contexts). */
+FFWD_B200_API long long ffwd_b200_launch_count(void);
+/* Last error message of the calling thread ("" if none). */
+FFWD_B200_API const char *ffwd_b200_last_error(void);
+/* Precision plan chosen at load: 0 = bf16, 2 = split-bf16 2-pass, 3 = 3-pass. */
+FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx);
+
+/* Host-side LPT partition used by the sharder: assigns each of n items with
+ * cost[i] to one of n_parts parts, minimising the largest part.  Writes
+ * part[i].  Exposed for tests. */
+FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts, int *part);
+
+/* Operator-level entry for tests: Y = X W^T with the tcgen05 GEMM on device
+ * pointers (bf16 X [M, K], bf16 W [N, K], f32 Y [M, N]) on the stream of
+ * device index 0 of no context (the current device, default stream).  bn is
+ * 128 or 256.  x_lo / w_lo select the 2- / 3-pass split form when non-NULL. */
+FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const void *w,
+                                      const void *w_lo, float *y, int M, int N, int K, int bn);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FFWD_B200_H */

@@ -1,0 +1,81 @@
+"""ctypes binding to the reference's own CPU forward (oracle/_ref/libffwd_ref.so).
+
+TEST INFRASTRUCTURE ONLY: the checker and the timed CPU baseline.  The library
+is built from the unmodified reference sources by oracle/Makefile and wraps
+``ffwd_model_load`` / ``ffwd_model_encode_batch`` (libffwd/forward.c:628-652).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_ref", "libffwd_ref.so")
+_lib = None
+
+
+def available() -> bool:
+    return os.path.exists(LIB_PATH)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        l = ctypes.CDLL(LIB_PATH)
+        l.ref_load.restype = ctypes.c_void_p
+        l.ref_load.argtypes = [ctypes.c_char_p]
+        l.ref_free.argtypes = [ctypes.c_void_p]
+        l.ref_set_threads.argtypes = [ctypes.c_int]
+        l.ref_config.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        l.ref_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                 ctypes.c_void_p]
+        l.ref_forward.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        _lib = l
+    return _lib
+
+
+class RefModel:
+    def __init__(self, model_dir: str, threads: int = 1):
+        self.l = lib()
+        self.l.ref_set_threads(int(threads))
+        self.h = self.l.ref_load(model_dir.encode())
+        if not self.h:
+            raise RuntimeError(f"reference failed to load {model_dir}")
+        ints = np.zeros(18, dtype=np.int32)
+        floats = np.zeros(3, dtype=np.float32)
+        self.l.ref_config(self.h, ints.ctypes.data, floats.ctypes.data)
+        self.ints, self.floats = ints, floats
+        self.hidden = int(ints[2])
+
+    def set_threads(self, n: int):
+        self.l.ref_set_threads(int(n))
+
+    def encode_batch(self, seqs) -> np.ndarray:
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(s, np.int32) for s in seqs]))
+        lens = np.ascontiguousarray(np.array([len(s) for s in seqs], dtype=np.int32))
+        out = np.zeros((len(seqs), self.hidden), dtype=np.float32)
+        rc = self.l.ref_encode(self.h, ids.ctypes.data, lens.ctypes.data, len(seqs), out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError("reference encode failed")
+        return out
+
+    def forward_states(self, ids) -> np.ndarray:
+        ids = np.ascontiguousarray(np.asarray(ids, np.int32))
+        out = np.zeros((len(ids), self.hidden), dtype=np.float32)
+        if self.l.ref_forward(self.h, ids.ctypes.data, len(ids), out.ctypes.data) != 0:
+            raise RuntimeError("reference forward failed")
+        return out
+
+    def close(self):
+        if self.h:
+            self.l.ref_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

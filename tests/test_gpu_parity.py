@@ -1,0 +1,168 @@
+"""End-to-end parity of the B200 forward (through the C ABI) against the
+reference's CPU path: the golden fixtures it produced, and the CPU checker on
+further seeded batches.  Gates: f32 mode max-abs <= 1e-4
+and cosine >= 0.99999 per row; bf16 mode cosine >= 0.999 per row."""
+
+import numpy as np
+import pytest
+
+from ffwd_b200 import native, synth
+from oracle import forward as of
+
+from golden_util import fixtures, load
+from helpers import small_spec, small_batch, cos_rows
+
+pytestmark = pytest.mark.gpu
+
+F32_MAXABS = 1e-4
+F32_COS = 0.99999
+BF16_COS = 0.999
+
+_models = {}
+
+
+def model(d, gemm_mode, weight_dtype=None):
+    key = (d, gemm_mode, weight_dtype)
+    if key not in _models:
+        _models[key] = native.B200Model(d, gemm_mode=gemm_mode, weight_dtype=weight_dtype)
+    return _models[key]
+
+
+def check(out, ref, exact):
+    cos = cos_rows(out, ref)
+    if exact:
+        err = np.abs(out - ref).max()
+        assert err <= F32_MAXABS, f"max-abs {err}"
+        assert cos.min() >= F32_COS, f"cos {cos.min()}"
+    else:
+        assert cos.min() >= BF16_COS, f"cos {cos.min()}"
+    assert np.isfinite(out).all()
+
+
+@pytest.mark.parametrize("name", fixtures())
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_golden(name, mode, model_root):
+    spec, d, seqs, expected = load(name, model_root)
+    m = model(d, mode)
+    out = m.encode_batch(seqs)
+    exact = m.precision != 0
+    # Decoders with bf16 weights run 16-bit regardless of the GEMM mode
+    # (libffwd/cuda.cu:5010-5019); everything else follows the mode.
+    if spec.family in ("qwen3", "qwen2") and spec.dtype == "bf16":
+        assert m.precision == 0
+    elif mode == "f32":
+        assert m.precision in (2, 3)
+    check(out, expected, exact)
+
+
+@pytest.mark.parametrize("key", ["qwen3-f32-2l", "minilm-2l", "bge-2l"])
+def test_exact_mode_longer_batches(key, model_root):
+    s = small_spec(key)
+    d = synth.ensure_model(s, model_root)
+    seqs = small_batch(key, n=5, max_len=260, seed=3)
+    ref = of.OracleModel(d).encode_batch(seqs)
+    m = model(d, "f32")
+    assert m.precision == 3
+    check(m.encode_batch(seqs), ref, True)
+
+
+def test_qwen_long_and_ragged(model_root):
+    s = small_spec("qwen3-2l")
+    d = synth.ensure_model(s, model_root)
+    rng = np.random.default_rng(5)
+    lens = [1, 3, 64, 127, 128, 129, 255, 256, 300, 700]
+    seqs = [rng.integers(0, s.vocab, size=L).astype(np.int32) for L in lens]
+    ref = of.OracleModel(d).encode_batch(seqs)
+    out = model(d, "bf16").encode_batch(seqs)
+    check(out, ref, False)
+
+
+def test_packed_equals_singleton_bitwise(model_root):
+    s = small_spec("qwen3-2l")
+    d = synth.ensure_model(s, model_root)
+    m = model(d, "bf16")
+    seqs = small_batch("qwen3-2l", n=4, max_len=200, seed=9)
+    packed = m.encode_batch(seqs)
+    single = np.stack([m.encode_into(q) for q in seqs])
+    assert np.array_equal(packed, single)
+
+
+def test_deterministic_repeats(model_root):
+    s = small_spec("bge-bf16-2l")
+    d = synth.ensure_model(s, model_root)
+    m = model(d, "bf16")
+    seqs = small_batch("bge-bf16-2l", n=8, max_len=300, seed=2)
+    a = m.encode_batch(seqs)
+    b = m.encode_batch(seqs)
+    c = m.encode_batch(seqs)
+    assert np.array_equal(a, b) and np.array_equal(b, c)
+
+
+def test_invalid_inputs_rejected(model_root):
+    s = small_spec("minilm-2l")
+    d = synth.ensure_model(s, model_root)
+    m = model(d, "f32")
+    rc, _ = m.try_encode_batch([np.array([101, s.vocab, 102], np.int32)])
+    assert rc == -1 and "invalid token id" in native.last_error()
+    rc, _ = m.try_encode_batch([np.array([101, -1, 102], np.int32)])
+    assert rc == -1
+    rc, _ = m.try_encode_batch([np.zeros(0, np.int32)])
+    assert rc == -1
+    rc, _ = m.try_encode_batch([np.full(513, 1000, np.int32)])
+    assert rc == -1 and "max_position_embeddings" in native.last_error()
+    # the context stays usable after a rejected call
+    seqs = small_batch("minilm-2l", n=2)
+    ref = of.OracleModel(d).encode_batch(seqs)
+    check(m.encode_batch(seqs), ref, True)
+
+
+def test_xlmr_max_length_512(model_root):
+    # position offset 2: 512 tokens fit max_position_embeddings 514 exactly
+    s = small_spec("xlmr-2l")
+    d = synth.ensure_model(s, model_root)
+    seqs = synth.token_batch("xlmr-large", batch=2, vocab=s.vocab)
+    ref = of.OracleModel(d).encode_batch(seqs)
+    check(model(d, "bf16").encode_batch(seqs), ref, False)
+    rc, _ = model(d, "bf16").try_encode_batch([np.full(513, 5, np.int32)])
+    assert rc == -1
+
+
+def test_spans_match_checker(model_root):
+    s = small_spec("qwen3-2l")
+    d = synth.ensure_model(s, model_root)
+    docs = small_batch("qwen3-2l", n=2, max_len=180, seed=4)
+    spans = [[(0, 10), (5, 50), (len(docs[0]) - 1, 1)], [(0, len(docs[1]))]]
+    om = of.OracleModel(d)
+    ref = []
+    for doc, sp in zip(docs, spans):
+        x, offs = om.hidden_states([doc])
+        x = of.rms_norm(x, om.t["norm.weight"], om.cfg["rms_eps"])
+        for a, n in sp:
+            ref.append(x[a:a + n].mean(0))
+    ref = np.stack(ref)
+    out = model(d, "bf16").encode_spans_batch(docs, spans)
+    cos = cos_rows(out, ref)
+    assert cos.min() >= BF16_COS
+
+
+def test_max_tokens_chunking_matches(model_root):
+    s = small_spec("bge-bf16-2l")
+    d = synth.ensure_model(s, model_root)
+    seqs = small_batch("bge-bf16-2l", n=12, max_len=200, seed=6)
+    whole = model(d, "bf16").encode_batch(seqs)
+    native.lib().ffwd_b200_set_max_tokens(300)
+    try:
+        chunked = native.B200Model(d, gemm_mode="bf16").encode_batch(seqs)
+    finally:
+        native.lib().ffwd_b200_set_max_tokens(65536)
+    assert np.array_equal(whole, chunked)
+
+
+def test_public_api_matches_abi(model_root):
+    s = small_spec("bge-bf16-2l")
+    d = synth.ensure_model(s, model_root)
+    seqs = small_batch("bge-bf16-2l", n=3)
+    a = native.FfwdApi(d, gemm_mode="bf16")
+    out = a.encode_batch(seqs)
+    a.close()
+    assert np.array_equal(out, model(d, "bf16").encode_batch(seqs))

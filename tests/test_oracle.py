@@ -1,0 +1,72 @@
+"""The CPU checker against the reference: golden fixtures produced by the
+reference's own CPU path, the compiled reference itself (when built), and the
+reference's kernel known-answer values (tests/test_kernels.c:96-127)."""
+
+import numpy as np
+import pytest
+
+from oracle import forward as of
+from oracle import ref as oref
+
+from golden_util import fixtures, load
+from helpers import small_spec, small_batch, cos_rows
+from ffwd_b200 import synth
+
+
+@pytest.mark.parametrize("name", fixtures())
+def test_oracle_matches_reference_golden(name, model_root):
+    spec, d, seqs, expected = load(name, model_root)
+    out = of.OracleModel(d).encode_batch(seqs)
+    assert out.shape == expected.shape
+    assert np.abs(out - expected).max() <= 2e-6, name
+    assert cos_rows(out, expected).min() >= 0.999999
+
+
+@pytest.mark.skipif(not oref.available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("name", fixtures())
+def test_compiled_reference_reproduces_golden(name, model_root):
+    spec, d, seqs, expected = load(name, model_root)
+    r = oref.RefModel(d, threads=2)
+    out = r.encode_batch(seqs)
+    r.close()
+    assert np.abs(out - expected).max() <= 1e-6
+
+
+def test_gelu_known_values():
+    # tests/test_kernels.c:106-126
+    x = np.array([1.0], np.float32)
+    assert abs(float(of.gelu(x, "erf")[0]) - 0.841344746) < 1e-6
+    assert abs(float(of.gelu(x, "tanh")[0]) - 0.841191991) < 1e-6
+
+
+def test_norms_known_values():
+    x = np.array([[1.0, 2.0, 3.0, 4.0]], np.float32)
+    w = np.ones(4, np.float32)
+    r = of.rms_norm(x, w, np.float32(1e-6))
+    assert np.allclose(r, x / np.sqrt(7.5 + 1e-6), atol=1e-6)
+    ln = of.layer_norm(x, w, np.zeros(4, np.float32), np.float32(1e-12))
+    assert np.allclose(ln, (x - 2.5) / np.sqrt(1.25), atol=1e-6)
+
+
+def test_packed_equals_singleton_oracle(model_root):
+    # test_qwen3.c:39-81: packed batch == per-sequence encode (<= 1e-5)
+    s = small_spec("qwen3-2l")
+    d = synth.ensure_model(s, model_root)
+    m = of.OracleModel(d)
+    seqs = small_batch("qwen3-2l", n=3, max_len=90)
+    packed = m.encode_batch(seqs)
+    single = np.stack([m.encode_batch([q])[0] for q in seqs])
+    assert np.abs(packed - single).max() <= 1e-5
+    assert np.allclose(np.linalg.norm(packed, axis=1), 1.0, atol=1e-5)
+
+
+def test_oracle_rejects_bad_inputs(model_root):
+    s = small_spec("minilm-2l")
+    d = synth.ensure_model(s, model_root)
+    m = of.OracleModel(d)
+    with pytest.raises(ValueError):
+        m.encode_batch([np.array([101, s.vocab + 5, 102], np.int32)])
+    with pytest.raises(ValueError):
+        m.encode_batch([np.zeros(0, np.int32)])
+    with pytest.raises(ValueError):
+        m.encode_batch([np.full(600, 1000, np.int32)])
