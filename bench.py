@@ -1,0 +1,472 @@
+"""Benchmark: embedded tokens/s of the packed embedding forward on B200.
+
+Workload (the one the headline metric is quoted on):
+Qwen3-Embedding-0.6B-shaped decoder, bf16, random-init safetensors weights
+(seed 0); per rank a batch of 128 sequences, lengths U[32, 2048] + EOS, token
+ids U[0, 151642] (seed 1 + rank).  One step = one forward + last-token pooling
++ L2 over that batch.  Weak scaling: every rank (one per GPU) encodes its own
+batch; value = all ranks' tokens / max-over-ranks time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` is measured with the inputs resident in HBM (ffwd_b200_encode_device)
+and CUDA events on the backend's stream; `e2e` goes through the reference's
+public API (ffwd_encode_batch of libffwd_b200_api.so) with host token ids,
+H2D / D2H inside the timed region.  `--impl reference` times the reference's
+own CPU path (oracle/_ref, OpenBLAS f32) on a bounded sample of the workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from ffwd_b200 import synth  # noqa: E402
+
+CONFIG = "qwen3-0.6b"
+METRIC = "embedded tokens/s"
+UNIT = "tokens/s"
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def workload(rank: int):
+    spec = synth.CONFIGS[CONFIG]
+    seqs = synth.token_batch(CONFIG, seed=1 + rank)
+    return spec, seqs
+
+
+def flops_per_token(spec, seqs):
+    """Algorithmic FLOPs (2 x MAC), attention causal-exact, token-weighted."""
+    H, I, L = spec.hidden, spec.intermediate, spec.n_layers
+    q = spec.n_heads * spec.head_dim
+    kv = spec.n_kv_heads * spec.head_dim
+    lin = 2.0 * L * (H * (q + 2 * kv) + q * H + 3 * H * I)
+    lens = np.array([len(s) for s in seqs], np.float64)
+    attn = L * 4.0 * q * ((lens * (lens + 1) / 2).sum()) / lens.sum()
+    return lin + attn, lin, attn
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        loaded = [v for v in sm if mx and v > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ distributed
+
+
+class Dist:
+    def __init__(self):
+        self.world = env_int("WORLD_SIZE", 1)
+        self.rank = env_int("RANK", 0)
+        self.local = env_int("LOCAL_RANK", 0)
+        self.pg = False
+
+    def init(self, torch):
+        if self.world > 1:
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+            self.pg = True
+
+    def barrier(self, torch):
+        if self.pg:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, torch, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, torch, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ CPU reference
+
+
+def cpu_reference_sample(model_dir, seqs, budget_s):
+    """Time the reference CPU path on the leading sequences of the batch that
+    fit ~budget_s.  Returns (tokens/s, tokens, seconds, n_seqs, threads)."""
+    from oracle.ref import RefModel
+    threads = os.cpu_count() or 1
+    ref = RefModel(model_dir, threads=threads)
+    probe = [seqs[0][:64]]
+    t0 = time.perf_counter()
+    ref.encode_batch(probe)  # warm-up: page in the weights
+    t0 = time.perf_counter()
+    ref.encode_batch(probe)
+    per_tok = (time.perf_counter() - t0) / len(probe[0])
+    n, tok = 0, 0
+    while n < len(seqs):
+        L = len(seqs[n])
+        # attention grows with L; scale the probe rate by length / 64 beyond the linear part
+        est = per_tok * (tok + L) * (1.0 + (tok + L) / 4096.0)
+        if n > 0 and est > budget_s:
+            break
+        tok += L
+        n += 1
+    sample = seqs[:n]
+    t0 = time.perf_counter()
+    ref.encode_batch(sample)
+    dt = time.perf_counter() - t0
+    ref.close()
+    return tok / dt, tok, dt, n, threads
+
+
+def run_reference(args, dist):
+    if dist.rank != 0:
+        return 0
+    spec, seqs = workload(0)
+    d = synth.ensure_model(spec)
+    from oracle import ref as oref
+    if not oref.available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libffwd_ref.so not built (make -C oracle)"}))
+        return 0
+    from oracle.ref import RefModel
+    threads = os.cpu_count() or 1
+    ref = RefModel(d, threads=threads)
+    # Size one step (a bounded sample) from a probe so K + W steps take minutes.
+    probe = [seqs[0][:64]]
+    ref.encode_batch(probe)
+    t0 = time.perf_counter()
+    ref.encode_batch(probe)
+    per_tok = (time.perf_counter() - t0) / 64
+    budget = max(2.0, 150.0 / (args.steps + args.warmup))
+    n, tok = 0, 0
+    while n < len(seqs):
+        L = len(seqs[n])
+        if n > 0 and per_tok * (tok + L) * (1.0 + (tok + L) / 4096.0) > budget:
+            break
+        tok += L
+        n += 1
+    sample = seqs[:n]
+    for _ in range(args.warmup):
+        ref.encode_batch(sample)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ref.encode_batch(sample)
+        times.append(time.perf_counter() - t0)
+    ref.close()
+    total = sum(times)
+    value = tok * len(times) / total
+    sample_desc = (f"first {n} of the 128 seeded sequences ({tok} tokens) per step, "
+                   f"reference CPU path (OpenBLAS f32, bf16 weights widened) on {threads} threads")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded ids, random-init weights)",
+        "config": {"workload": "Qwen3-Embedding-0.6B bf16, 128 seqs U[32,2048]+EOS, last-token+L2",
+                   "sample_tokens_per_step": tok},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": sample_desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ ours
+
+
+def read_traffic():
+    """DRAM bytes per launch of the gate/up GEMM from the committed ncu summary
+    (profiles/gemm_gate_up_qwen3_0.6b.md, key `dram_bytes_per_token`)."""
+    p = os.path.join(ROOT, "profiles", "gemm_gate_up_qwen3_0.6b.md")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"dram_bytes_per_token\s*[:=]\s*([0-9.eE+-]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+def run_ours(args, dist):
+    import torch
+    from ffwd_b200 import native
+
+    dist.init(torch)
+    dev = dist.local if dist.world > 1 else 0
+    torch.cuda.set_device(dev)
+    spec, seqs = workload(dist.rank)
+    if dist.rank == 0:
+        d = synth.ensure_model(spec)
+    dist.barrier(torch)
+    d = synth.ensure_model(spec)
+
+    peaks = {}
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peaks = json.load(open(pk))
+    peak_tflops = peaks.get("bf16_tflops")
+    peak_kind = "measured (burst)" if peak_tflops else "fallback"
+    peak_tflops = peak_tflops or 1590.0
+
+    m = native.B200Model(d, gemm_mode="bf16", devices=[dev])
+    lens = np.array([len(s) for s in seqs], np.int32)
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T, B, H = int(offs[-1]), len(seqs), spec.hidden
+    ids = np.concatenate(seqs).astype(np.int32)
+    d_ids = torch.from_numpy(ids).to(f"cuda:{dev}")
+    d_out = torch.empty((B, H), dtype=torch.float32, device=f"cuda:{dev}")
+    stream = torch.cuda.ExternalStream(m.stream(), device=f"cuda:{dev}")
+
+    def step():
+        m.encode_device(d_ids.data_ptr(), offs, d_out.data_ptr(), sync=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---------------- device-resident timed region
+    clocks = ClockSampler(dev)
+    dist.barrier(torch)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.4)
+    n0 = native.launch_count()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    launches = native.launch_count() - n0
+    torch.cuda.synchronize()
+    dist.barrier(torch)
+    clk = clocks.stop()
+    local_s = e0.elapsed_time(e1) / 1000.0
+    max_s = dist.max(torch, local_s)
+    total_tokens = dist.sum(torch, float(T))
+    value = total_tokens * args.steps / max_s
+    ms_per_step = 1000.0 * max_s / args.steps
+
+    # ---------------- per-kernel timing (CUDA events on the backend's stream)
+    reps = 10
+    ops = {0: "gemm_qkv_qknorm_rope", 1: "attention_varlen_causal", 2: "gemm_o_resid",
+           3: "rmsnorm", 4: "gemm_gate_up_swiglu", 5: "gemm_down_resid", 6: "rmsnorm"}
+    op_ms = {}
+    for op in (0, 1, 2, 3, 4, 5):
+        m.run_op(op, layer=0, reps=2)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        m.run_op(op, layer=0, reps=reps)
+        b.record(stream)
+        b.synchronize()
+        op_ms[ops[op]] = a.elapsed_time(b) / reps
+    q = spec.n_heads * spec.head_dim
+    kv = spec.n_kv_heads * spec.head_dim
+    gu_flops = 2.0 * T * (2 * spec.intermediate) * H
+    gu_s = op_ms["gemm_gate_up_swiglu"] / 1000.0
+    achieved = gu_flops / gu_s / 1e12
+    traffic_per_tok = read_traffic()
+    fpt, lin_fpt, attn_fpt = flops_per_token(spec, seqs)
+    kernels = {
+        "gemm_qkv_qknorm_rope": 2.0 * T * (q + 2 * kv) * H,
+        "gemm_o_resid": 2.0 * T * H * q,
+        "gemm_gate_up_swiglu": gu_flops,
+        "gemm_down_resid": 2.0 * T * H * spec.intermediate,
+        "attention_varlen_causal": 4.0 * q * float((lens.astype(np.float64) *
+                                                   (lens + 1) / 2).sum()),
+    }
+    kernel_report = {k: {"ms": round(op_ms[k], 4),
+                         "tflops": round(kernels[k] / (op_ms[k] / 1000.0) / 1e12, 1),
+                         "frac_of_peak": round(kernels[k] / (op_ms[k] / 1000.0) / 1e12
+                                               / peak_tflops, 3)}
+                     for k in kernels}
+    kernel_report["rmsnorm"] = {"ms": round(op_ms["rmsnorm"], 4),
+                                "gbs": round(T * H * 6 / (op_ms["rmsnorm"] / 1000.0) / 1e9, 1)}
+    model_tflops = T * fpt / (ms_per_step / 1000.0) / 1e12
+
+    # ---------------- end to end through the public API (host buffers)
+    os.environ["FFWD_B200_DEVICES"] = str(dev)
+    m.close()
+    del m
+    api = native.FfwdApi(d, gemm_mode="bf16")
+    ins = (native.ffwd_input_t * B)()
+    keep = [np.ascontiguousarray(s, dtype=np.int32) for s in seqs]
+    for i, a in enumerate(keep):
+        ins[i].ids = a.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+        ins[i].n_tokens = len(a)
+    out = np.zeros((B, H), np.float32)
+    for _ in range(max(1, args.warmup)):
+        assert api.encode_batch_into(ins, B, out.ctypes.data) == 0
+    dist.barrier(torch)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        assert api.encode_batch_into(ins, B, out.ctypes.data) == 0
+    e2e_local = time.perf_counter() - t0
+    e2e_max = dist.max(torch, e2e_local)
+    e2e_value = total_tokens * args.steps / e2e_max
+    n_items = int(sum((L + 127) // 128 for L in lens))
+    h2d = T * 4 + (B + 1) * 4 + n_items * 8
+    d2h = B * H * 4 + 4
+
+    # p50 micro-batch latency, server packing (length-sorted, <= 32 inputs,
+    # <= 16384 tokens; tools/server/handlers.c:51-120, models.c:269-276)
+    order = sorted(range(B), key=lambda i: len(seqs[i]))
+    batches, cur, ctok = [], [], 0
+    for i in order:
+        L = len(seqs[i])
+        if cur and (len(cur) >= 32 or ctok + L > 16384):
+            batches.append(cur)
+            cur, ctok = [], 0
+        cur.append(i)
+        ctok += L
+    if cur:
+        batches.append(cur)
+    lat = []
+    for bi, bidx in enumerate(batches):
+        sub = (native.ffwd_input_t * len(bidx))()
+        for j, i in enumerate(bidx):
+            sub[j] = ins[i]
+        o = np.zeros((len(bidx), H), np.float32)
+        api.encode_batch_into(sub, len(bidx), o.ctypes.data)  # warm this shape
+        t0 = time.perf_counter()
+        assert api.encode_batch_into(sub, len(bidx), o.ctypes.data) == 0
+        lat.append((time.perf_counter() - t0) * 1000.0)
+    api.close()
+
+    # ---------------- CPU baseline (rank 0, N = 1)
+    cpu = None
+    if dist.world == 1 and not args.no_cpu:
+        from oracle import ref as oref
+        if oref.available():
+            v, tok, dt, n, thr = cpu_reference_sample(d, seqs, budget_s=args.cpu_budget)
+            cpu = {"value": v, "unit": UNIT, "cores": thr, "kind": "reference",
+                   "sample": f"first {n} of the 128 seeded sequences ({tok} tokens, {dt:.1f} s), "
+                             f"reference CPU path (OpenBLAS f32) via oracle/_ref"}
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded token ids, random-init bf16 safetensors weights)",
+            "config": {
+                "workload": "Qwen3-Embedding-0.6B bf16 (28 layers, hidden 1024, 16/8 heads x 128, "
+                            "SwiGLU 3072), 128 seqs/GPU U[32,2048]+EOS, last-token pooling + L2",
+                "tokens_per_gpu_step": T, "sequences_per_gpu_step": B,
+                "parallelism": f"dp{dist.world} (sequence sharding, no collective)",
+                "l2": "inputs larger than L2 (weights 1.2 GB, activations > 1 GB per step)",
+            },
+            "p50_batch_latency_ms": statistics.median(lat) if lat else None,
+            "model_tflops": model_tflops,
+            "gflop_per_token": fpt / 1e9,
+            "roofline": {
+                "kernel": "gemm_gate_up_swiglu (tcgen05, fused SwiGLU epilogue)",
+                "bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
+                "frac": achieved / peak_tflops, "peak_source": peak_kind,
+                "flops_per_launch": gu_flops,
+                "traffic": (traffic_per_tok * T) if traffic_per_tok else None,
+            },
+            "kernels": kernel_report,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "ffwd_encode_batch (libffwd_b200_api.so)"},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    dist.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    dist = Dist()
+    if args.impl == "reference":
+        return run_reference(args, dist)
+    return run_ours(args, dist)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -146,6 +146,26 @@ struct Workspace {
     float *h_out = nullptr;
 };
 
+// Per-forward state: shapes, activation tensor maps and the attention work
+// list of the forward last prepared on a device (also lets single ops be
+// re-issued for timing).
+struct FwdState {
+    int T = 0, B = 0, n_items = 0;
+    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv;
+    AttnParams ap{};
+};
+
+enum Op : int {
+    kOpQKV = 0,
+    kOpAttn = 1,
+    kOpO = 2,
+    kOpNorm1 = 3,
+    kOpUp = 4,
+    kOpDown = 5,
+    kOpNorm2 = 6,
+    kOpCount = 7,
+};
+
 struct Device {
     int dev = 0;
     int num_sms = 148;
@@ -158,6 +178,7 @@ struct Device {
     int rope_cap = 0;
     std::vector<LayerW> layers;
     Workspace ws;
+    FwdState fs;
     std::vector<void *> allocs;
 };
 
@@ -564,18 +585,20 @@ int gemm(Device &D, int prec, const CUtensorMap *a, const CUtensorMap *a_lo, con
     return 0;
 }
 
-// The forward over the packed rows already uploaded to D.ws (ids, offsets on
-// device; h_offsets on host).  Leaves final hidden states in ws.x.
-int forward(ffwd_b200_ctx *ctx, Device &D, int T, int B, const int *h_offsets) {
+// Upload-independent preparation: RoPE cache, attention items, tensor maps,
+// positions and the embedding (+ first norm).  ws.ids / ws.offsets must hold
+// the packed batch; h_offsets is its host copy.
+int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int *h_offsets) {
     const ffwd_config_t &c = ctx->cfg;
     Workspace &w = D.ws;
-    const int prec = ctx->prec;
-    const bool split = prec != 0;
+    const bool split = ctx->prec != 0;
     const int H = c.hidden_size, I = c.intermediate_size;
     const int qkv_dim = c.q_dim + 2 * c.kv_dim;
     const bool bert = c.family == FFWD_FAMILY_BERT;
     const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
     cudaStream_t s = D.stream;
+    fs.T = T;
+    fs.B = B;
 
     int max_len = 0;
     for (int b = 0; b < B; ++b) max_len = std::max(max_len, h_offsets[b + 1] - h_offsets[b]);
@@ -583,7 +606,6 @@ int forward(ffwd_b200_ctx *ctx, Device &D, int T, int B, const int *h_offsets) {
 
     // Attention work list, heaviest first.
     const int qt = split ? attention_f32_qtile(c.head_dim) : 128;
-    int n_items = 0;
     {
         std::vector<std::pair<int, AttnItem>> items;
         for (int b = 0; b < B; ++b) {
@@ -602,38 +624,26 @@ int forward(ffwd_b200_ctx *ctx, Device &D, int T, int B, const int *h_offsets) {
         for (size_t i = 0; i < items.size(); ++i) w.h_items[i] = items[i].second;
         CK(cudaMemcpyAsync(w.items, w.h_items, items.size() * sizeof(AttnItem),
                            cudaMemcpyHostToDevice, s));
-        n_items = (int)items.size();
+        fs.n_items = (int)items.size();
     }
 
-    // Activation tensor maps for this T.
-    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv;
-    if (make_map(&m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        make_map(&m_att, w.att, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        make_map(&m_h, w.hmid, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (make_map(&fs.m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&fs.m_att, w.att, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&fs.m_h, w.hmid, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
-    if (split && (make_map(&m_xb_lo, w.xb_lo, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-                  make_map(&m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-                  make_map(&m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
+    if (split && (make_map(&fs.m_xb_lo, w.xb_lo, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  make_map(&fs.m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
         return -1;
-    if (!split && make_map(&m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
+    if (!split && make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
         return -1;
 
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
-
-    LAUNCH((positions_kernel<<<B, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0, w.pos),
-            cudaGetLastError()));
-    if (bert)
-        LAUNCH(embed_ln_launch(w.ids, w.pos, T, D.embed, D.embed_bf16, c.vocab_size, D.pos_table,
-                               D.type0, D.emb_ln_g, D.emb_ln_b, H, eps, w.x, xb_out, w.err, s));
-    else
-        LAUNCH(embed_rms_launch(w.ids, T, D.embed, D.embed_bf16, c.vocab_size, H, w.x,
-                                D.layers[0].in_norm, eps, xb_out, w.err, s));
-
-    AttnParams ap{};
+    AttnParams &ap = fs.ap;
+    ap = AttnParams{};
     ap.offsets = w.offsets;
     ap.items = w.items;
-    ap.n_items = n_items;
+    ap.n_items = fs.n_items;
     ap.n_heads = c.n_heads;
     ap.n_kv_heads = c.n_kv_heads;
     ap.head_dim = c.head_dim;
@@ -650,87 +660,124 @@ int forward(ffwd_b200_ctx *ctx, Device &D, int T, int B, const int *h_offsets) {
     ap.out_lo = w.att_lo;
     ap.err = w.err;
 
-    for (int li = 0; li < c.n_layers; ++li) {
-        const LayerW &l = D.layers[li];
-        // ---- QKV projection (+ bias, + QK-norm and RoPE on the decoder)
-        {
-            GemmParams p{};
-            p.M = T;
-            p.out = w.qkv;
-            p.ldo = qkv_dim;
-            p.out_mode = split ? kOutF32 : kOutBF16;
-            p.bias = l.b_qkv;
-            p.err = w.err;
-            if (bert) {
-                p.epi = kEpiStore;
-            } else {
-                p.epi = kEpiQKRope;
-                p.pos = w.pos;
-                p.rope_cos = D.rope_cos;
-                p.rope_sin = D.rope_sin;
-                p.q_norm = l.q_norm;
-                p.k_norm = l.k_norm;
-                p.n_q_heads = c.n_heads;
-                p.n_kv_heads = c.n_kv_heads;
-                p.head_dim = c.head_dim;
-                p.eps = c.rms_norm_eps;
-            }
-            if (gemm(D, prec, &m_xb, &m_xb_lo, l.qkv, p)) return -1;
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
+    LAUNCH((positions_kernel<<<B, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0, w.pos),
+            cudaGetLastError()));
+    if (bert)
+        LAUNCH(embed_ln_launch(w.ids, w.pos, T, D.embed, D.embed_bf16, c.vocab_size, D.pos_table,
+                               D.type0, D.emb_ln_g, D.emb_ln_b, H, eps, w.x, xb_out, w.err, s));
+    else
+        LAUNCH(embed_rms_launch(w.ids, T, D.embed, D.embed_bf16, c.vocab_size, H, w.x,
+                                D.layers[0].in_norm, eps, xb_out, w.err, s));
+    return 0;
+}
+
+// One op of layer li on the prepared forward.
+int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
+    const ffwd_config_t &c = ctx->cfg;
+    Workspace &w = D.ws;
+    const int prec = ctx->prec;
+    const bool split = prec != 0;
+    const int H = c.hidden_size, I = c.intermediate_size, T = fs.T;
+    const int qkv_dim = c.q_dim + 2 * c.kv_dim;
+    const bool bert = c.family == FFWD_FAMILY_BERT;
+    const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
+    cudaStream_t s = D.stream;
+    const LayerW &l = D.layers[li];
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
+    switch (op) {
+    case kOpQKV: {  // QKV projection (+ bias, + QK-norm and RoPE on the decoder)
+        GemmParams p{};
+        p.M = T;
+        p.out = w.qkv;
+        p.ldo = qkv_dim;
+        p.out_mode = split ? kOutF32 : kOutBF16;
+        p.bias = l.b_qkv;
+        p.err = w.err;
+        if (bert) {
+            p.epi = kEpiStore;
+        } else {
+            p.epi = kEpiQKRope;
+            p.pos = w.pos;
+            p.rope_cos = D.rope_cos;
+            p.rope_sin = D.rope_sin;
+            p.q_norm = l.q_norm;
+            p.k_norm = l.k_norm;
+            p.n_q_heads = c.n_heads;
+            p.n_kv_heads = c.n_kv_heads;
+            p.head_dim = c.head_dim;
+            p.eps = c.rms_norm_eps;
         }
-        // ---- attention
+        return gemm(D, prec, &fs.m_xb, &fs.m_xb_lo, l.qkv, p);
+    }
+    case kOpAttn:
         if (split)
-            LAUNCH(attention_f32_launch(ap, s));
+            LAUNCH(attention_f32_launch(fs.ap, s));
         else
-            LAUNCH(attention_tc_launch(&m_qkv, ap, s));
-        // ---- output projection + residual (+ bias)
-        {
-            GemmParams p{};
-            p.M = T;
-            p.epi = kEpiResid;
-            p.resid = w.x;
-            p.ldr = H;
-            p.bias = l.b_o;
-            p.err = w.err;
-            if (gemm(D, prec, &m_att, &m_att_lo, l.o, p)) return -1;
-        }
+            LAUNCH(attention_tc_launch(&fs.m_qkv, fs.ap, s));
+        return 0;
+    case kOpO: {  // output projection + residual (+ bias)
+        GemmParams p{};
+        p.M = T;
+        p.epi = kEpiResid;
+        p.resid = w.x;
+        p.ldr = H;
+        p.bias = l.b_o;
+        p.err = w.err;
+        return gemm(D, prec, &fs.m_att, &fs.m_att_lo, l.o, p);
+    }
+    case kOpNorm1:
         if (bert)
             LAUNCH(layernorm_launch(w.x, T, H, l.ln1_g, l.ln1_b, eps, xb_out, s));
         else
             LAUNCH(rmsnorm_launch(w.x, T, H, l.post_norm, eps, xb_out, s));
-        // ---- FFN up (GELU) or gate/up (SwiGLU)
-        {
-            GemmParams p{};
-            p.M = T;
-            p.out = w.hmid;
-            p.out_lo = w.hmid_lo;
-            p.ldo = I;
-            p.out_mode = split ? kOutSplit : kOutBF16;
-            p.err = w.err;
-            if (bert) {
-                p.epi = kEpiGelu;
-                p.bias = l.b_up;
-                p.gelu_tanh = c.ffn_act == FFWD_ACT_GELU_TANH;
-            } else {
-                p.epi = kEpiSwiGLU;
-            }
-            if (gemm(D, prec, &m_xb, &m_xb_lo, l.up, p)) return -1;
+        return 0;
+    case kOpUp: {  // FFN up (GELU) or gate/up (SwiGLU)
+        GemmParams p{};
+        p.M = T;
+        p.out = w.hmid;
+        p.out_lo = w.hmid_lo;
+        p.ldo = I;
+        p.out_mode = split ? kOutSplit : kOutBF16;
+        p.err = w.err;
+        if (bert) {
+            p.epi = kEpiGelu;
+            p.bias = l.b_up;
+            p.gelu_tanh = c.ffn_act == FFWD_ACT_GELU_TANH;
+        } else {
+            p.epi = kEpiSwiGLU;
         }
-        // ---- FFN down + residual (+ bias)
-        {
-            GemmParams p{};
-            p.M = T;
-            p.epi = kEpiResid;
-            p.resid = w.x;
-            p.ldr = H;
-            p.bias = l.b_down;
-            p.err = w.err;
-            if (gemm(D, prec, &m_h, &m_h_lo, l.down, p)) return -1;
-        }
+        return gemm(D, prec, &fs.m_xb, &fs.m_xb_lo, l.up, p);
+    }
+    case kOpDown: {  // FFN down + residual (+ bias)
+        GemmParams p{};
+        p.M = T;
+        p.epi = kEpiResid;
+        p.resid = w.x;
+        p.ldr = H;
+        p.bias = l.b_down;
+        p.err = w.err;
+        return gemm(D, prec, &fs.m_h, &fs.m_h_lo, l.down, p);
+    }
+    case kOpNorm2:
         if (bert)
             LAUNCH(layernorm_launch(w.x, T, H, l.ln2_g, l.ln2_b, eps, xb_out, s));
         else if (li + 1 < c.n_layers)
             LAUNCH(rmsnorm_launch(w.x, T, H, D.layers[li + 1].in_norm, eps, xb_out, s));
+        return 0;
     }
+    fail("unknown op %d", op);
+    return -1;
+}
+
+// The forward over the packed rows already uploaded to D.ws (ids, offsets on
+// device; h_offsets on host).  Leaves final hidden states in ws.x.
+int forward(ffwd_b200_ctx *ctx, Device &D, int T, int B, const int *h_offsets) {
+    FwdState &fs = D.fs;
+    if (prepare(ctx, D, fs, T, B, h_offsets)) return -1;
+    for (int li = 0; li < ctx->cfg.n_layers; ++li)
+        for (int op = 0; op < kOpCount; ++op)
+            if (step(ctx, D, fs, op, li)) return -1;
     return 0;
 }
 
@@ -1167,6 +1214,24 @@ FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const i
         CK(cudaStreamSynchronize(D.stream));
         if (check_err(D)) return -1;
     }
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_run_op(ffwd_b200_ctx_t *ctx, int dev, int op, int layer, int reps) {
+    t_err.clear();
+    if (!ctx || dev < 0 || dev >= (int)ctx->devs.size() || op < 0 || op >= kOpCount || layer < 0 ||
+        layer >= ctx->cfg.n_layers || reps < 1) {
+        fail("invalid arguments");
+        return -1;
+    }
+    Device &D = ctx->devs[dev];
+    if (D.fs.T <= 0) {
+        fail("no prepared forward on device %d", dev);
+        return -1;
+    }
+    CK(cudaSetDevice(D.dev));
+    for (int r = 0; r < reps; ++r)
+        if (step(ctx, D, D.fs, op, layer)) return -1;
     return 0;
 }
 

@@ -74,6 +74,8 @@ ABI = {
                                                ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                                ctypes.c_int]),
     "ffwd_b200_stream": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int]),
+    "ffwd_b200_run_op": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int]),
     "ffwd_b200_launch_count": (ctypes.c_longlong, []),
     "ffwd_b200_last_error": (ctypes.c_char_p, []),
     "ffwd_b200_precision": (ctypes.c_int, [ctypes.c_void_p]),
@@ -230,6 +232,10 @@ class B200Model:
                                              d_out, 1 if sync else 0)
         if rc != 0:
             raise FfwdError(f"encode_device failed: {last_error()}")
+
+    def run_op(self, op: int, layer: int = 0, reps: int = 1, dev: int = 0):
+        if self._l.ffwd_b200_run_op(self.h, dev, op, layer, reps) != 0:
+            raise FfwdError(f"run_op failed: {last_error()}")
 
     def stream(self, dev: int = 0) -> int:
         return self._l.ffwd_b200_stream(self.h, dev) or 0

@@ -160,6 +160,13 @@ FFWD_B200_API int ffwd_b200_set_max_tokens(int max_tokens);
 FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const int *d_ids,
                                           const int *h_offsets, int batch, float *d_out, int sync);
 
+/* Re-issue `reps` launches of one op of layer `layer` on the buffers of the
+ * last forward run on device index dev (enqueued, not synchronised), for
+ * per-kernel timing: 0 QKV projection, 1 attention, 2 output projection,
+ * 3 first norm, 4 FFN up / gate-up, 5 FFN down, 6 second norm.  Ops that
+ * accumulate into the residual stream change the buffers' values. */
+FFWD_B200_API int ffwd_b200_run_op(ffwd_b200_ctx_t *ctx, int dev, int op, int layer, int reps);
+
 /* The CUDA stream (cudaStream_t) the context uses on device index dev. */
 FFWD_B200_API void *ffwd_b200_stream(ffwd_b200_ctx_t *ctx, int dev);
 /* Kernel launches issued by this process since load (all contexts). */
