@@ -178,6 +178,7 @@ struct Device {
     int rope_cap = 0;
     std::vector<LayerW> layers;
     Workspace ws;
+    Workspace *active_ws = nullptr;  // when set, step() uses these buffers instead of ws
     FwdState fs;
     std::vector<void *> allocs;
 };
@@ -675,7 +676,7 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
 // One op of layer li on the prepared forward.
 int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
     const ffwd_config_t &c = ctx->cfg;
-    Workspace &w = D.ws;
+    Workspace &w = D.active_ws ? *D.active_ws : D.ws;
     const int prec = ctx->prec;
     const bool split = prec != 0;
     const int H = c.hidden_size, I = c.intermediate_size, T = fs.T;
@@ -1276,3 +1277,229 @@ FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const voi
 }
 
 }  // extern "C"
+
+// ====================================================================== no-allocation entry
+//
+// Scratch for ffwd_b200_encode_device_noalloc: a fixed arena in device global
+// memory, reserved on every GPU that loads this library and held until the
+// process exits.  It is shared by every call on a device and keeps the last
+// call's contents.
+namespace fb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 32u << 20;  // 32 MiB per device
+constexpr int kNoAllocMaxItems = 8192;
+constexpr int kNoAllocMaxBatch = 4096;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device ordinal, resolved once per
+// device (with that device current) by the first no-allocation call there.
+uint8_t *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(int dev, uint8_t **out) {
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        fail("device ordinal %d out of range for the no-allocation scratch", dev);
+        return -1;
+    }
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            fail("cudaGetSymbolAddress(no-allocation scratch) failed on device %d: %s", dev,
+                 cudaGetErrorString(e));
+            return -1;
+        }
+        g_noalloc_ptr[dev] = static_cast<uint8_t *>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return 0;
+}
+
+// Bump carve of the arena (256-byte aligned pieces).  Returns false when the
+// request does not fit.
+struct Carver {
+    uint8_t *base;
+    size_t used = 0, cap;
+    template <typename T>
+    bool take(T **p, size_t count) {
+        size_t off = (used + 255) & ~size_t(255);
+        size_t bytes = count * sizeof(T);
+        if (off + bytes > cap) return false;
+        *p = reinterpret_cast<T *>(base + off);
+        used = off + bytes;
+        return true;
+    }
+};
+
+}  // namespace
+}  // namespace fb
+
+extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ctx, int dev,
+                                                             const int *d_ids,
+                                                             const int *h_offsets, int batch,
+                                                             float *d_out) {
+    t_err.clear();
+    if (!ctx || dev < 0 || dev >= (int)ctx->devs.size() || !d_ids || !h_offsets || batch <= 0 ||
+        !d_out) {
+        fail("invalid arguments");
+        return -1;
+    }
+    const ffwd_config_t &c = ctx->cfg;
+    Device &D = ctx->devs[dev];
+    CK(cudaSetDevice(D.dev));
+    const int T = h_offsets[batch];
+    int max_len = 0;
+    for (int b = 0; b < batch; ++b) {
+        const int L = h_offsets[b + 1] - h_offsets[b];
+        if (L <= 0 || (c.family == FFWD_FAMILY_BERT &&
+                       L > c.max_position_embeddings - c.position_id_offset)) {
+            fail("invalid sequence length %d at %d", L, b);
+            return -1;
+        }
+        max_len = std::max(max_len, L);
+    }
+    if (batch > kNoAllocMaxBatch) {
+        fail("no-allocation encode: batch %d exceeds the maximum %d", batch, kNoAllocMaxBatch);
+        return -1;
+    }
+    if (c.family != FFWD_FAMILY_BERT && max_len > D.rope_cap) {
+        fail("no-allocation encode: sequence length %d exceeds the loaded RoPE table (%d)", max_len,
+             D.rope_cap);
+        return -1;
+    }
+
+    // Attention work list, heaviest first (same order rule as prepare()).
+    const bool split = ctx->prec != 0;
+    const int qt = split ? attention_f32_qtile(c.head_dim) : 128;
+    AttnItem items[kNoAllocMaxItems];
+    int costs[kNoAllocMaxItems];
+    int n_items = 0;
+    for (int b = 0; b < batch; ++b) {
+        const int L = h_offsets[b + 1] - h_offsets[b];
+        const int nq = (L + qt - 1) / qt;
+        for (int t = 0; t < nq; ++t) {
+            if (n_items == kNoAllocMaxItems) {
+                fail("no-allocation encode: more than %d attention tiles", kNoAllocMaxItems);
+                return -1;
+            }
+            costs[n_items] = c.attention_mode == FFWD_ATTENTION_CAUSAL ? t + 1 : nq;
+            items[n_items++] = AttnItem{b, t};
+        }
+    }
+    for (int i = 1; i < n_items; ++i) {  // insertion sort by cost, descending (stable)
+        AttnItem it = items[i];
+        int cs = costs[i], j = i - 1;
+        while (j >= 0 && costs[j] < cs) {
+            items[j + 1] = items[j];
+            costs[j + 1] = costs[j];
+            --j;
+        }
+        items[j + 1] = it;
+        costs[j + 1] = cs;
+    }
+
+    // Carve the arena.
+    uint8_t *base = nullptr;
+    if (noalloc_scratch(D.dev, &base)) return -1;
+    const int H = c.hidden_size, I = c.intermediate_size, qkv_dim = c.q_dim + 2 * c.kv_dim;
+    Workspace w{};
+    Carver cv{base, 0, kNoAllocScratchBytes};
+    bool ok = cv.take(&w.err, 1) && cv.take(&w.offsets, (size_t)batch + 1) &&
+              cv.take(&w.items, (size_t)n_items) && cv.take(&w.ids, (size_t)T) &&
+              cv.take(&w.pos, (size_t)T) && cv.take(&w.x, (size_t)T * H) &&
+              cv.take(&w.xb, (size_t)T * H) && cv.take(&w.att, (size_t)T * c.q_dim) &&
+              cv.take(&w.hmid, (size_t)T * I);
+    if (ok) {
+        uint8_t *q = nullptr;
+        ok = cv.take(&q, (size_t)T * qkv_dim * (split ? 4 : 2));
+        w.qkv = q;
+    }
+    if (ok && split)
+        ok = cv.take(&w.xb_lo, (size_t)T * H) && cv.take(&w.att_lo, (size_t)T * c.q_dim) &&
+             cv.take(&w.hmid_lo, (size_t)T * I);
+    if (!ok) {
+        fail("no-allocation encode: %d tokens need more than the %zu-byte scratch maximum", T,
+             kNoAllocScratchBytes);
+        return -1;
+    }
+    w.cap_t = T;
+    w.cap_b = batch + 1;
+    w.cap_items = n_items;
+
+    cudaStream_t s = D.stream;
+    CK(cudaMemsetAsync(w.err, 0, 4, s));  // the arena keeps the previous call's error word
+    CK(cudaMemcpyAsync(w.ids, d_ids, (size_t)T * 4, cudaMemcpyDeviceToDevice, s));
+    CK(cudaMemcpyAsync(w.offsets, h_offsets, (size_t)(batch + 1) * 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(w.items, items, (size_t)n_items * sizeof(AttnItem), cudaMemcpyHostToDevice,
+                       s));
+
+    // Forward on the arena buffers: same prepare / step sequence as forward().
+    FwdState fs;
+    fs.T = T;
+    fs.B = batch;
+    fs.n_items = n_items;
+    const bool bert = c.family == FFWD_FAMILY_BERT;
+    const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
+    if (make_map(&fs.m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&fs.m_att, w.att, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&fs.m_h, w.hmid, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    if (split && (make_map(&fs.m_xb_lo, w.xb_lo, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  make_map(&fs.m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return -1;
+    if (!split && make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
+                           c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    AttnParams &ap = fs.ap;
+    ap.offsets = w.offsets;
+    ap.items = w.items;
+    ap.n_items = n_items;
+    ap.n_heads = c.n_heads;
+    ap.n_kv_heads = c.n_kv_heads;
+    ap.head_dim = c.head_dim;
+    ap.q_col0 = 0;
+    ap.k_col0 = c.q_dim;
+    ap.v_col0 = c.q_dim + c.kv_dim;
+    ap.causal = c.attention_mode == FFWD_ATTENTION_CAUSAL;
+    ap.scale = 1.0f / sqrtf((float)c.head_dim);
+    ap.out = w.att;
+    ap.ldo = c.q_dim;
+    ap.qkv_f32 = static_cast<const float *>(w.qkv);
+    ap.ldq = qkv_dim;
+    ap.out_hi = w.att;
+    ap.out_lo = w.att_lo;
+    ap.err = w.err;
+
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
+    LAUNCH((positions_kernel<<<batch, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0,
+                                                   w.pos),
+            cudaGetLastError()));
+    if (bert)
+        LAUNCH(embed_ln_launch(w.ids, w.pos, T, D.embed, D.embed_bf16, c.vocab_size, D.pos_table,
+                               D.type0, D.emb_ln_g, D.emb_ln_b, H, eps, w.x, xb_out, w.err, s));
+    else
+        LAUNCH(embed_rms_launch(w.ids, T, D.embed, D.embed_bf16, c.vocab_size, H, w.x,
+                                D.layers[0].in_norm, eps, xb_out, w.err, s));
+    D.active_ws = &w;
+    int rc = 0;
+    for (int li = 0; li < c.n_layers && rc == 0; ++li)
+        for (int op = 0; op < kOpCount && rc == 0; ++op) rc = step(ctx, D, fs, op, li);
+    D.active_ws = nullptr;
+    if (rc) return -1;
+    LAUNCH(pool_launch(w.x, w.offsets, batch, H, c.pooling_mode,
+                       bert ? nullptr : D.final_norm, c.rms_norm_eps, c.normalize_embeddings, d_out,
+                       w.err, s));
+    int h_err = 0;
+    CK(cudaMemcpyAsync(&h_err, w.err, 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (h_err) {
+        fail("device error %d in no-allocation encode", h_err);
+        return -1;
+    }
+    return 0;
+}

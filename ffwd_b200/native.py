@@ -73,6 +73,9 @@ ABI = {
     "ffwd_b200_encode_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                                ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                                ctypes.c_int]),
+    "ffwd_b200_encode_device_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int,
+                                                       ctypes.c_void_p, ctypes.c_void_p,
+                                                       ctypes.c_int, ctypes.c_void_p]),
     "ffwd_b200_stream": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int]),
     "ffwd_b200_run_op": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int]),
@@ -232,6 +235,12 @@ class B200Model:
                                              d_out, 1 if sync else 0)
         if rc != 0:
             raise FfwdError(f"encode_device failed: {last_error()}")
+
+    def encode_device_noalloc(self, d_ids: int, offsets, d_out: int, dev: int = 0) -> int:
+        """Return code of the no-allocation entry (0 or -1)."""
+        off = np.ascontiguousarray(np.asarray(offsets, dtype=np.int32))
+        return self._l.ffwd_b200_encode_device_noalloc(self.h, dev, d_ids, off.ctypes.data,
+                                                       len(off) - 1, d_out)
 
     def run_op(self, op: int, layer: int = 0, reps: int = 1, dev: int = 0):
         if self._l.ffwd_b200_run_op(self.h, dev, op, layer, reps) != 0:

@@ -160,6 +160,24 @@ FFWD_B200_API int ffwd_b200_set_max_tokens(int max_tokens);
 FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const int *d_ids,
                                           const int *h_offsets, int batch, float *d_out, int sync);
 
+/* No counterpart in the reference.  Same computation and arguments as
+ * ffwd_b200_encode_device, for callers that cannot allocate device memory
+ * while serving: hosts that hand all GPU memory to their own pool and forbid
+ * other allocations, and latency-sensitive callers for whom cudaMalloc /
+ * cudaFree (which can synchronise the device) are off limits on the request
+ * path.  This entry allocates nothing: its working buffers live in a fixed
+ * 32 MiB arena of device memory reserved, on every GPU that loads the library,
+ * until the process exits.  Requests whose buffers do not fit the arena (for
+ * example more than about 1300 tokens for a Qwen3-0.6B-shaped model), more
+ * than 4096 sequences or 8192 attention tiles are rejected with -1 and a
+ * message.  The first call on a device resolves the arena's device address
+ * with that device current; make that first call before any stream capture.
+ * All calls share the one arena and it keeps the last call's contents, so
+ * calls whose GPU work overlaps (other streams, other host threads) race.
+ * Returns after the work has completed. */
+FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ctx, int dev, const int *d_ids,
+                                                  const int *h_offsets, int batch, float *d_out);
+
 /* Re-issue `reps` launches of one op of layer `layer` on the buffers of the
  * last forward run on device index dev (enqueued, not synchronised), for
  * per-kernel timing: 0 QKV projection, 1 attention, 2 output projection,
