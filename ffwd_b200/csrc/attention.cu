@@ -1,26 +1,33 @@
 // Varlen attention kernels (see attention.cuh).
 //
-// Tensor-core kernel, one CTA per (query tile of 128 rows, head):
-//   warp 0      TMA producer: Q tile once, then K_j / V_j key tiles (128 keys)
-//               into a two-deep ring.
-//   warp 1      allocates TMEM; one lane issues S_j = Q K_j^T (tcgen05.mma,
-//               M=128 N=128, into one of two TMEM score buffers) one tile ahead
-//               of the softmax, and O_j = P_j V_j (M=128, N=head_dim, V read as
-//               an MN-major operand straight from its TMA tile).
-//   warps 2-5   softmax, one thread per query row: reads its score row from
-//               TMEM, applies the length / causal mask and the online-softmax
-//               update, writes P_j as bf16 into a 128-byte-swizzled shared
-//               tile for the next MMA, and folds O_j into f32 registers.
+// Tensor-core kernel, one CTA per work item = up to two query blocks (128
+// query rows of one head each) that share one key/value head; 384 threads:
+//   warp 0      TMA producer: both Q tiles once, then K_0 V_0 K_1 V_1 ... into a
+//               three-slot shared-memory ring.
+//   warp 1      allocates TMEM (S0 | S1 | O0 | O1) and one lane issues the
+//               tcgen05.mma: S_w = Q_w K_j^T (M=128, N=128) and O_w += P_w V_j
+//               (M=128, N=head_dim, V read as an MN-major operand from its TMA
+//               tile), interleaving the two blocks so the tensor cores work on
+//               one block while the other block's softmax runs.
+//   warps 4-7   softmax for block 0, warps 8-11 for block 1: one thread per
+//               query row reads its score row from TMEM, masks (length, causal),
+//               writes P_w = exp2(s - m) as bf16 into a 128-byte-swizzled shared
+//               tile and keeps the row sum.  O stays in TMEM; it is rescaled in
+//               place only when the running row max grows by more than 2^8.
 // Masking follows the packed layout: key k of sequence b is visible to query q
 // iff k < len(b) and (bidirectional or k <= q).
 #include "attention.cuh"
 #include "ptx.cuh"
 
+#include <algorithm>
+
 namespace fb {
 namespace {
 
 constexpr int kTile = 128;  // query rows and keys per tile
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 384;
+constexpr int kRingSlots = 3;
+constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
 
 template <int D>
 struct AttnCfg {
@@ -32,12 +39,11 @@ struct AttnCfg {
     static constexpr int BOX_BYTES = kTile * ROWB;
     static constexpr int TILE_BYTES = NBOX * BOX_BYTES;              // Q, K or V tile
     static constexpr int P_BYTES = kTile * kTile * 2;                // 2 SW128 blocks
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + TILE_BYTES;
-    static constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;
-    static constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;
-    static constexpr int SMEM = OFF_P + P_BYTES + 1024;
-    static constexpr int TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) O [256, 256 + D)
+    static constexpr int OFF_Q = 0;                                  // Q0, Q1
+    static constexpr int OFF_RING = 2 * TILE_BYTES;
+    static constexpr int OFF_P = OFF_RING + kRingSlots * TILE_BYTES; // P0, P1
+    static constexpr int SMEM = OFF_P + 2 * P_BYTES + 1024;
+    static constexpr int TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D, ..)
 };
 
 // K-major operand (Q or K tile): k-step `kk` covers elements [16 kk, 16 kk + 16).
@@ -55,9 +61,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     using C = AttnCfg<D>;
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t q_full;
-    __shared__ __align__(8) uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-    __shared__ __align__(8) uint64_t s_full[2], s_free[2];
-    __shared__ __align__(8) uint64_t p_full, o_full, o_free, drain;
+    __shared__ __align__(8) uint64_t ring_full[kRingSlots], ring_empty[kRingSlots];
+    __shared__ __align__(8) uint64_t s_full[2], p_full[2], o_final[2];
+    __shared__ __align__(8) uint64_t drain;
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
@@ -67,27 +73,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
     const AttnItem item = p.items[blockIdx.x];
-    const int h = blockIdx.y;
-    const int kvh = h / (p.n_heads / p.n_kv_heads);
+    const bool two = item.qt1 >= 0;
+    const int kvh = item.h0 / (p.n_heads / p.n_kv_heads);
     const int seq0 = p.offsets[item.seq];
     const int L = p.offsets[item.seq + 1] - seq0;
-    const int q0 = item.qtile * kTile;
-    const int kend = p.causal ? min(q0 + kTile, L) : L;
+    const int qt_max = two ? max(item.qt0, item.qt1) : item.qt0;
+    const int kend = p.causal ? min(qt_max * kTile + kTile, L) : L;
     const int n_kt = (kend + kTile - 1) / kTile;
 
     if (threadIdx.x == 0) {
         mbar_init(&q_full, 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&k_empty[i], 1);
-            mbar_init(&v_full[i], 1);
-            mbar_init(&v_empty[i], 1);
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
+        for (int i = 0; i < kRingSlots; ++i) {
+            mbar_init(&ring_full[i], 1);
+            mbar_init(&ring_empty[i], 1);
         }
-        mbar_init(&p_full, 4);
-        mbar_init(&o_full, 1);
-        mbar_init(&o_free, 4);
+        for (int w = 0; w < 2; ++w) {
+            mbar_init(&s_full[w], 1);
+            mbar_init(&p_full[w], 4);
+            mbar_init(&o_final[w], 1);
+        }
         mbar_init(&drain, 1);
         abort_sh = 0;
         fence_barrier_init();
@@ -103,196 +107,242 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t tmem_base = tmem_base_sh;
 
     uint8_t *sQ = smem + C::OFF_Q;
-    uint8_t *sK = smem + C::OFF_K;
-    uint8_t *sV = smem + C::OFF_V;
+    uint8_t *sRing = smem + C::OFF_RING;
     uint8_t *sP = smem + C::OFF_P;
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued_k = 0, issued_v = 0;
+            // ------------------------------------------------------------ producer
+            int issued = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(&q_full, C::TILE_BYTES);
+            mbar_arrive_expect_tx(&q_full, (two ? 2 : 1) * C::TILE_BYTES);
             for (int b = 0; b < C::NBOX; ++b)
-                tma_load_2d(sQ + b * C::BOX_BYTES, &tm, &q_full, p.q_col0 + h * D + b * C::BOXC,
-                            seq0 + q0);
-            for (int j = 0; j < n_kt && ok; ++j) {
-                const int s = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                const int row = seq0 + j * kTile;
-                if (!mbar_wait(&k_empty[s], ph ^ 1, p.err, &abort_sh)) { ok = false; break; }
-                mbar_arrive_expect_tx(&k_full[s], C::TILE_BYTES);
+                tma_load_2d(sQ + b * C::BOX_BYTES, &tm, &q_full,
+                            p.q_col0 + item.h0 * D + b * C::BOXC, seq0 + item.qt0 * kTile);
+            if (two)
                 for (int b = 0; b < C::NBOX; ++b)
-                    tma_load_2d(sK + s * C::TILE_BYTES + b * C::BOX_BYTES, &tm, &k_full[s],
-                                p.k_col0 + kvh * D + b * C::BOXC, row);
-                ++issued_k;
-                if (!mbar_wait(&v_empty[s], ph ^ 1, p.err, &abort_sh)) { ok = false; break; }
-                mbar_arrive_expect_tx(&v_full[s], C::TILE_BYTES);
+                    tma_load_2d(sQ + C::TILE_BYTES + b * C::BOX_BYTES, &tm, &q_full,
+                                p.q_col0 + item.h1 * D + b * C::BOXC, seq0 + item.qt1 * kTile);
+            for (int i = 0; i < 2 * n_kt; ++i) {
+                const int slot = i % kRingSlots;
+                const uint32_t ph = (i / kRingSlots) & 1;
+                if (!mbar_wait(&ring_empty[slot], ph ^ 1, p.err, &abort_sh)) {
+                    ok = false;
+                    break;
+                }
+                const int col = ((i & 1) ? p.v_col0 : p.k_col0) + kvh * D;
+                const int row = seq0 + (i >> 1) * kTile;
+                mbar_arrive_expect_tx(&ring_full[slot], C::TILE_BYTES);
                 for (int b = 0; b < C::NBOX; ++b)
-                    tma_load_2d(sV + s * C::TILE_BYTES + b * C::BOX_BYTES, &tm, &v_full[s],
-                                p.v_col0 + kvh * D + b * C::BOXC, row);
-                ++issued_v;
+                    tma_load_2d(sRing + slot * C::TILE_BYTES + b * C::BOX_BYTES, &tm,
+                                &ring_full[slot], col + b * C::BOXC, row);
+                ++issued;
             }
             if (!ok) {
                 mbar_wait(&q_full, 0, nullptr, nullptr);
-                for (int j = issued_k - 2 < 0 ? 0 : issued_k - 2; j < issued_k; ++j)
-                    mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
-                for (int j = issued_v - 2 < 0 ? 0 : issued_v - 2; j < issued_v; ++j)
-                    mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
+                for (int i = issued - kRingSlots < 0 ? 0 : issued - kRingSlots; i < issued; ++i)
+                    mbar_wait(&ring_full[i % kRingSlots], (i / kRingSlots) & 1, nullptr, nullptr);
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
             constexpr uint32_t IDESC_S = idesc_f16(128, 128, 1, 1, 0, 0);
             constexpr uint32_t IDESC_O = idesc_f16(128, D, 1, 1, 0, 1);
             const uint32_t aQ = smem_u32(sQ);
-            bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh);
-            auto issue_s = [&](int j) -> bool {
-                const int s = j & 1;
-                if (!mbar_wait(&k_full[s], (j >> 1) & 1, p.err, &abort_sh)) return false;
-                if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, p.err, &abort_sh)) return false;
-                tc_fence_after();
-                const uint32_t aK = smem_u32(sK + s * C::TILE_BYTES);
+            const uint32_t aRing = smem_u32(sRing);
+            const uint32_t aP = smem_u32(sP);
+            const int nw = two ? 2 : 1;
+            auto slot_of = [](int i) { return i % kRingSlots; };
+            auto wait_slot = [&](int i) -> bool {
+                return mbar_wait(&ring_full[i % kRingSlots], (i / kRingSlots) & 1, p.err, &abort_sh);
+            };
+            auto issue_s = [&](int w, int j) {
+                const uint32_t aK = aRing + slot_of(2 * j) * C::TILE_BYTES;
+                const uint32_t aQw = aQ + w * C::TILE_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(tmem_base + s * 128, kmajor_desc<D>(aQ, kk), kmajor_desc<D>(aK, kk),
+                    umma_f16(tmem_base + w * 128, kmajor_desc<D>(aQw, kk), kmajor_desc<D>(aK, kk),
                              IDESC_S, kk != 0);
-                umma_commit(&s_full[s]);
-                umma_commit(&k_empty[s]);
-                return true;
             };
-            if (ok && n_kt > 0) ok = issue_s(0);
-            for (int j = 0; ok && j < n_kt; ++j) {
-                if (j + 1 < n_kt && !issue_s(j + 1)) { ok = false; break; }
-                const int s = j & 1;
-                if (!mbar_wait(&p_full, j & 1, p.err, &abort_sh)) { ok = false; break; }
-                if (!mbar_wait(&v_full[s], (j >> 1) & 1, p.err, &abort_sh)) { ok = false; break; }
-                if (!mbar_wait(&o_free, (j & 1) ^ 1, p.err, &abort_sh)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t aP = smem_u32(sP);
-                const uint32_t aV = smem_u32(sV + s * C::TILE_BYTES);
+            auto issue_pv = [&](int w, int j) {
+                const uint32_t aV = aRing + slot_of(2 * j + 1) * C::TILE_BYTES;
+                const uint32_t aPw = aP + w * C::P_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < kTile / 16; ++kk) {
-                    // P: K-major over keys, two 64-key SW128 blocks.
-                    const uint64_t pd = smem_desc(aP + (kk / 4) * (kTile * 128) + (kk % 4) * 32, 16,
+                    const uint64_t pd = smem_desc(aPw + (kk / 4) * (kTile * 128) + (kk % 4) * 32, 16,
                                                   1024, kLayoutSW128);
-                    // V: MN-major (N = head_dim), 16 key rows per k-step.
                     const uint64_t vd = smem_desc(aV + kk * 16 * C::ROWB, C::BOX_BYTES, C::SBO,
                                                   C::LAYOUT);
-                    umma_f16(tmem_base + 256, pd, vd, IDESC_O, kk != 0);
+                    umma_f16(tmem_base + 256 + w * D, pd, vd, IDESC_O, (j | kk) != 0);
                 }
-                umma_commit(&o_full);
-                umma_commit(&v_empty[s]);
+            };
+            bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh) && wait_slot(0);
+            if (ok) {
+                tc_fence_after();
+                for (int w = 0; w < nw; ++w) {
+                    issue_s(w, 0);
+                    umma_commit(&s_full[w]);
+                }
+                umma_commit(&ring_empty[slot_of(0)]);
+            }
+            for (int j = 0; ok && j < n_kt; ++j) {
+                const bool more = j + 1 < n_kt;
+                if (!wait_slot(2 * j + 1)) {
+                    ok = false;
+                    break;
+                }
+                for (int w = 0; w < nw; ++w) {
+                    if (!mbar_wait(&p_full[w], j & 1, p.err, &abort_sh)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv(w, j);
+                    if (more) {
+                        if (w == 0 && !wait_slot(2 * j + 2)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        issue_s(w, j + 1);
+                        umma_commit(&s_full[w]);
+                    } else {
+                        umma_commit(&o_final[w]);
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&ring_empty[slot_of(2 * j + 1)]);
+                if (more) umma_commit(&ring_empty[slot_of(2 * j + 2)]);
             }
             if (!ok) {
-                // Wait for the MMAs already issued before TMEM is released.
                 umma_commit(&drain);
                 mbar_wait(&drain, 0, nullptr, nullptr);
             }
         }
         __syncwarp();
-    } else {
-        // ------------------------------------------------------------ softmax
-        const int quad = warp & 3;
-        const int r = quad * 32 + lane;
-        const int q = q0 + r;
-        const float sl2 = p.scale * 1.4426950408889634f;
-        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-        float m = -1e30f, l = 0.0f, alpha_prev = 1.0f;
-        float acc[D];
-#pragma unroll
-        for (int i = 0; i < D; ++i) acc[i] = 0.0f;
-        bool ok = true;
-
-        auto fold_o = [&](int j) -> bool {
-            if (!mbar_wait(&o_full, j & 1, p.err, &abort_sh)) return false;
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                float t[32];
-                tmem_ld32(tmem_base + lane_off + 256 + c * 32, t);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) acc[c * 32 + i] = acc[c * 32 + i] * alpha_prev + t[i];
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&o_free);
-            return true;
-        };
-
-        for (int j = 0; j < n_kt; ++j) {
-            const int s = j & 1;
-            if (!mbar_wait(&s_full[s], (j >> 1) & 1, p.err, &abort_sh)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t sa = tmem_base + lane_off + s * 128;
-            const int k0 = j * kTile;
-            float mx = -INFINITY;
+    } else if (warp >= 4) {
+        // ---------------------------------------------------------------- softmax
+        const int w = (warp - 4) >> 2;  // block 0: warps 4-7, block 1: warps 8-11
+        if (w == 0 || two) {
+            const int quad = warp & 3;
+            const int r = quad * 32 + lane;
+            const int qt = w == 0 ? item.qt0 : item.qt1;
+            const int h = w == 0 ? item.h0 : item.h1;
+            const int q = qt * kTile + r;
+            const float sl2 = p.scale * 1.4426950408889634f;
+            const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+            const uint32_t tS = tmem_base + lane_off + w * 128;
+            const uint32_t tO = tmem_base + lane_off + 256 + w * D;
+            uint8_t *sPw = sP + w * C::P_BYTES;
+            float m_used = -INFINITY, l = 0.0f;
+            bool ok = true;
+            for (int j = 0; j < n_kt; ++j) {
+                if (!mbar_wait(&s_full[w], j & 1, p.err, &abort_sh)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int k0 = j * kTile;
+                // Tiles wholly inside the sequence and below the diagonal need no mask.
+                const bool masked = k0 + kTile > L || (p.causal && k0 + kTile - 1 > qt * kTile);
+                float mx = -INFINITY;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(sa + c * 32, v);
-                tmem_wait_ld();
+                for (int c = 0; c < 4; ++c) {
+                    float v[32];
+                    tmem_ld32(tS + c * 32, v);
+                    tmem_wait_ld();
+                    if (masked) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int key = k0 + c * 32 + i;
-                    const bool vis = key < L && (!p.causal || key <= q);
-                    mx = fmaxf(mx, vis ? v[i] * sl2 : -INFINITY);
+                        for (int i = 0; i < 32; ++i) {
+                            const int key = k0 + c * 32 + i;
+                            const bool vis = key < L && (!p.causal || key <= q);
+                            mx = fmaxf(mx, vis ? v[i] : -INFINITY);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+                    }
                 }
-            }
-            const float m_new = fmaxf(m, mx);
-            const float alpha = exp2f(m - m_new);
-            if (j > 0 && !fold_o(j - 1)) { ok = false; break; }
-            float sum = 0.0f;
+                const float m_new = fmaxf(m_used, mx * sl2);
+                // tcgen05.ld/st are warp-collective: the rescale decision is taken per
+                // warp (any row over the threshold), each row by its own factor.
+                if (j == 0) {
+                    m_used = m_new;
+                } else if (__any_sync(0xffffffffu, m_new > m_used + kRescaleLog2)) {
+                    // O_w is stable here: PV_{j-1} completed before S_j was published,
+                    // and PV_j waits for this block's P_j.
+                    const float alpha = exp2f(m_used - m_new);
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(sa + c * 32, v);
-                tmem_wait_ld();
-                uint32_t pk[16];
+                    for (int c = 0; c < D / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int key = k0 + c * 32 + 2 * i;
-                    const bool vis0 = key < L && (!p.causal || key <= q);
-                    const bool vis1 = key + 1 < L && (!p.causal || key + 1 <= q);
-                    const float p0 = vis0 ? exp2f(v[2 * i] * sl2 - m_new) : 0.0f;
-                    const float p1 = vis1 ? exp2f(v[2 * i + 1] * sl2 - m_new) : 0.0f;
-                    __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-                    // Row sum of the values the MMA will actually use.
-                    const float2 pf = __bfloat1622float2(pb);
-                    sum += pf.x + pf.y;
-                    pk[i] = *reinterpret_cast<uint32_t *>(&pb);
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(tO + c * 32, o);
+                    }
+                    tmem_wait_st();
+                    l *= alpha;
+                    m_used = m_new;
                 }
-                // Keys [32c, 32c + 32) -> block c/2, 16-byte chunks 4(c%2) .. +3.
-                uint8_t *rowp = sP + (c >> 1) * (kTile * 128) + r * 128;
+                float sum = 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    float v[32];
+                    tmem_ld32(tS + c * 32, v);
+                    tmem_wait_ld();
+                    uint32_t pk[16];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int chunk = (c & 1) * 4 + u;
-                    *reinterpret_cast<uint4 *>(rowp + ((chunk ^ (r & 7)) * 16)) =
-                        make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+                    for (int i = 0; i < 16; ++i) {
+                        float p0 = exp2f(fmaf(v[2 * i], sl2, -m_used));
+                        float p1 = exp2f(fmaf(v[2 * i + 1], sl2, -m_used));
+                        if (masked) {
+                            const int key = k0 + c * 32 + 2 * i;
+                            if (!(key < L && (!p.causal || key <= q))) p0 = 0.0f;
+                            if (!(key + 1 < L && (!p.causal || key + 1 <= q))) p1 = 0.0f;
+                        }
+                        __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+                        const float2 pf = __bfloat1622float2(pb);
+                        sum += pf.x + pf.y;
+                        pk[i] = *reinterpret_cast<uint32_t *>(&pb);
+                    }
+                    // Keys [32c, 32c + 32) -> block c/2, 16-byte chunks 4(c%2) .. +3.
+                    uint8_t *rowp = sPw + (c >> 1) * (kTile * 128) + r * 128;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int chunk = (c & 1) * 4 + u;
+                        *reinterpret_cast<uint4 *>(rowp + ((chunk ^ (r & 7)) * 16)) =
+                            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+                    }
+                }
+                l += sum;
+                tc_fence_before();
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[w]);
+            }
+            if (ok && mbar_wait(&o_final[w], 0, p.err, &abort_sh)) {
+                tc_fence_after();
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                __nv_bfloat16 *orow = p.out + (size_t)(seq0 + q) * p.ldo + h * D;
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    float o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+                    if (q < L) {
+                        uint4 *op = reinterpret_cast<uint4 *>(orow + c * 32);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
+                                               pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
+                                               pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
+                                               pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
+                    }
                 }
             }
-            l = l * alpha + sum;
-            tc_fence_before();
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&s_free[s]);
-                mbar_arrive(&p_full);
-            }
-            alpha_prev = alpha;
-            m = m_new;
-        }
-        if (ok && n_kt > 0) ok = fold_o(n_kt - 1);
-        if (ok && q < L) {
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            uint4 *o = reinterpret_cast<uint4 *>(p.out + (size_t)(seq0 + q) * p.ldo + h * D);
-#pragma unroll
-            for (int u = 0; u < D / 8; ++u)
-                o[u] = make_uint4(pack_bf16x2(acc[8 * u] * inv, acc[8 * u + 1] * inv),
-                                  pack_bf16x2(acc[8 * u + 2] * inv, acc[8 * u + 3] * inv),
-                                  pack_bf16x2(acc[8 * u + 4] * inv, acc[8 * u + 5] * inv),
-                                  pack_bf16x2(acc[8 * u + 6] * inv, acc[8 * u + 7] * inv));
         }
     }
 
@@ -323,10 +373,10 @@ __global__ void __launch_bounds__(kF32Threads)
     const int kvh = h / (p.n_heads / p.n_kv_heads);
     const int seq0 = p.offsets[item.seq];
     const int L = p.offsets[item.seq + 1] - seq0;
-    const int qi = item.qtile * QT + threadIdx.x / TPQ;
+    const int qi = item.qt0 * QT + threadIdx.x / TPQ;
     const int part = threadIdx.x % TPQ;
     const bool qvalid = qi < L;
-    const int kend = p.causal ? min(item.qtile * QT + QT, L) : L;
+    const int kend = p.causal ? min(item.qt0 * QT + QT, L) : L;
 
     float qv[DS], acc[DS];
     {
@@ -395,7 +445,7 @@ __global__ void __launch_bounds__(kF32Threads)
 
 int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStream_t stream) {
     if (p.n_items <= 0) return cudaSuccess;
-    dim3 grid(p.n_items, p.n_heads);
+    dim3 grid(p.n_items);
     cudaError_t e;
     switch (p.head_dim) {
     case 32:
@@ -434,6 +484,81 @@ int attention_f32_launch(const AttnParams &p, cudaStream_t stream) {
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+namespace {
+
+int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, const int *h_offsets,
+                          int batch) {
+    const int rep = n_heads / n_kv_heads;
+    long long n = 0;
+    for (int b = 0; b < batch; ++b) {
+        const int L = h_offsets[b + 1] - h_offsets[b];
+        if (!tc) {
+            n += ceil_div(L, attention_f32_qtile(head_dim));
+        } else if (rep >= 2) {
+            n += (long long)ceil_div(L, kTile) * n_kv_heads * ceil_div(rep, 2);
+        } else {
+            n += (long long)ceil_div(ceil_div(L, kTile), 2) * n_heads;
+        }
+    }
+    return n > 0x7fffffff ? -1 : (int)n;
+}
+
+int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int head_dim,
+                          const int *h_offsets, int batch, AttnItem *out, int cap) {
+    const int rep = n_heads / n_kv_heads;
+    int n = 0;
+    auto push = [&](const AttnItem &it) -> bool {
+        if (n >= cap) return false;
+        out[n++] = it;
+        return true;
+    };
+    for (int b = 0; b < batch; ++b) {
+        const int L = h_offsets[b + 1] - h_offsets[b];
+        if (!tc) {
+            const int qt = attention_f32_qtile(head_dim);
+            const int nq = ceil_div(L, qt);
+            for (int t = 0; t < nq; ++t)
+                if (!push(AttnItem{b, t, -1, -1, -1, causal ? t + 1 : nq})) return -1;
+            continue;
+        }
+        const int nq = ceil_div(L, kTile);
+        if (rep >= 2) {
+            // Two q-heads of one kv head share every K/V tile.
+            for (int t = 0; t < nq; ++t)
+                for (int g = 0; g < n_kv_heads; ++g)
+                    for (int pr = 0; pr < rep; pr += 2) {
+                        const int h0 = g * rep + pr;
+                        const bool has1 = pr + 1 < rep;
+                        const int kt = causal ? t + 1 : nq;
+                        if (!push(AttnItem{b, t, h0, has1 ? t : -1, has1 ? h0 + 1 : -1,
+                                           kt * (has1 ? 2 : 1)}))
+                            return -1;
+                    }
+        } else {
+            // Full multi-head: two query tiles of one head share the K/V stream.
+            for (int h = 0; h < n_heads; ++h)
+                for (int t = 0; t < nq; t += 2) {
+                    const bool has1 = t + 1 < nq;
+                    const int kt = causal ? (has1 ? t + 2 : t + 1) : nq;
+                    if (!push(AttnItem{b, t, h, has1 ? t + 1 : -1, has1 ? h : -1,
+                                       kt * (has1 ? 2 : 1)}))
+                        return -1;
+                }
+        }
+    }
+    std::sort(out, out + n, [](const AttnItem &x, const AttnItem &y) {
+        if (x.cost != y.cost) return x.cost > y.cost;
+        if (x.seq != y.seq) return x.seq < y.seq;
+        if (x.qt0 != y.qt0) return x.qt0 < y.qt0;
+        return x.h0 < y.h0;
+    });
+    return n;
 }
 
 }  // namespace fb

@@ -16,10 +16,15 @@
 
 namespace fb {
 
-// One work item = (sequence index, 128-row query tile); list sorted by cost.
+// One work item of a CTA.  Tensor-core path: up to two query blocks
+// (query tile, head) that share one key/value head, processed by the CTA's two
+// softmax warpgroups over one stream of K/V tiles; qt1 = -1 when the second
+// block is absent.  f32 path: (seq, qt0) with the head taken from blockIdx.y.
 struct AttnItem {
     int seq;
-    int qtile;
+    int qt0, h0;
+    int qt1, h1;
+    int cost;  // key tiles x blocks, for heaviest-first ordering
 };
 
 struct AttnParams {
@@ -40,6 +45,16 @@ struct AttnParams {
     __nv_bfloat16 *out_lo;
     int *err;
 };
+
+// Build the work list of a packed batch (host).  tc selects the tensor-core
+// pairing (128-row query tiles, two blocks per item) or the f32 path's items.
+// Writes at most cap items to out, sorted heaviest first (ties in a fixed
+// order); returns the count, or -1 if cap is too small.  Allocates nothing.
+int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int head_dim,
+                          const int *h_offsets, int batch, AttnItem *out, int cap);
+// Number of items attention_build_items would write.
+int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, const int *h_offsets,
+                          int batch);
 
 // Tensor-core path.  `qkv_map`: 2-D bf16 map over the qkv matrix with a box of
 // 128 rows x min(head_dim, 64) columns (128-byte swizzle, or 64-byte for

@@ -606,26 +606,18 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
     if (!bert && ensure_rope(D, c, max_len)) return -1;
 
     // Attention work list, heaviest first.
-    const int qt = split ? attention_f32_qtile(c.head_dim) : 128;
     {
-        std::vector<std::pair<int, AttnItem>> items;
-        for (int b = 0; b < B; ++b) {
-            const int L = h_offsets[b + 1] - h_offsets[b];
-            const int nq = (L + qt - 1) / qt;
-            for (int t = 0; t < nq; ++t) {
-                const int cost = c.attention_mode == FFWD_ATTENTION_CAUSAL ? t + 1 : nq;
-                items.push_back({cost, AttnItem{b, t}});
-            }
+        const int n = attention_count_items(!split, c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B);
+        if (n < 0 || ensure_ws(ctx, D, T, B, n, 0)) return -1;
+        fs.n_items = attention_build_items(!split, c.attention_mode == FFWD_ATTENTION_CAUSAL,
+                                           c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B,
+                                           w.h_items, w.cap_items);
+        if (fs.n_items < 0) {
+            fail("attention work list overflow");
+            return -1;
         }
-        std::stable_sort(items.begin(), items.end(),
-                         [](const std::pair<int, AttnItem> &x, const std::pair<int, AttnItem> &y) {
-                             return x.first > y.first;
-                         });
-        if (ensure_ws(ctx, D, T, B, (int)items.size(), 0)) return -1;
-        for (size_t i = 0; i < items.size(); ++i) w.h_items[i] = items[i].second;
-        CK(cudaMemcpyAsync(w.items, w.h_items, items.size() * sizeof(AttnItem),
+        CK(cudaMemcpyAsync(w.items, w.h_items, (size_t)fs.n_items * sizeof(AttnItem),
                            cudaMemcpyHostToDevice, s));
-        fs.n_items = (int)items.size();
     }
 
     if (make_map(&fs.m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1372,34 +1364,15 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
         return -1;
     }
 
-    // Attention work list, heaviest first (same order rule as prepare()).
+    // Attention work list, heaviest first (same builder as prepare()).
     const bool split = ctx->prec != 0;
-    const int qt = split ? attention_f32_qtile(c.head_dim) : 128;
     AttnItem items[kNoAllocMaxItems];
-    int costs[kNoAllocMaxItems];
-    int n_items = 0;
-    for (int b = 0; b < batch; ++b) {
-        const int L = h_offsets[b + 1] - h_offsets[b];
-        const int nq = (L + qt - 1) / qt;
-        for (int t = 0; t < nq; ++t) {
-            if (n_items == kNoAllocMaxItems) {
-                fail("no-allocation encode: more than %d attention tiles", kNoAllocMaxItems);
-                return -1;
-            }
-            costs[n_items] = c.attention_mode == FFWD_ATTENTION_CAUSAL ? t + 1 : nq;
-            items[n_items++] = AttnItem{b, t};
-        }
-    }
-    for (int i = 1; i < n_items; ++i) {  // insertion sort by cost, descending (stable)
-        AttnItem it = items[i];
-        int cs = costs[i], j = i - 1;
-        while (j >= 0 && costs[j] < cs) {
-            items[j + 1] = items[j];
-            costs[j + 1] = costs[j];
-            --j;
-        }
-        items[j + 1] = it;
-        costs[j + 1] = cs;
+    const int n_items = attention_build_items(!split, c.attention_mode == FFWD_ATTENTION_CAUSAL,
+                                              c.n_heads, c.n_kv_heads, c.head_dim, h_offsets,
+                                              batch, items, kNoAllocMaxItems);
+    if (n_items < 0) {
+        fail("no-allocation encode: more than %d attention work items", kNoAllocMaxItems);
+        return -1;
     }
 
     // Carve the arena.

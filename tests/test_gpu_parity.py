@@ -166,3 +166,16 @@ def test_public_api_matches_abi(model_root):
     out = a.encode_batch(seqs)
     a.close()
     assert np.array_equal(out, model(d, "bf16").encode_batch(seqs))
+
+
+def test_deep_long_sequences_rescale_path(model_root):
+    # Deeper random-init decoders grow the attention scores across key tiles,
+    # which drives the online-softmax rescale of O in TMEM (lanes of one warp
+    # disagree on whether to rescale).
+    s = synth.spec("qwen3-0.6b", n_layers=6, vocab=4096)
+    d = synth.ensure_model(s, model_root)
+    rng = np.random.default_rng(21)
+    lens = [2049, 1500, 900, 129, 33]
+    seqs = [rng.integers(0, s.vocab, size=L).astype(np.int32) for L in lens]
+    ref = of.OracleModel(d).encode_batch(seqs)
+    check(model(d, "bf16").encode_batch(seqs), ref, False)
