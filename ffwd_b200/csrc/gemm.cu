@@ -21,7 +21,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kEpiGroups = 2;  // epilogue warpgroups (split each tile's columns)
+constexpr int kThreads = 64 + 128 * kEpiGroups;
 
 template <int BN, int PASSES>
 struct GemmCfg {
@@ -92,11 +93,12 @@ __device__ __forceinline__ void store_row32(const GemmParams &p, int row, int co
 
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbase, int grow,
-                                              bool valid, int nb) {
+                                              bool valid, int nb, int g) {
+    // Warpgroup g of kEpiGroups handles every kEpiGroups-th unit of the tile.
     const int n0 = nb * BN;
     if constexpr (EPI == kEpiStore || EPI == kEpiGelu) {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = g; c < BN / 32; c += kEpiGroups) {
             float v[32];
             tmem_ld32(tbase + c * 32, v);
             tmem_wait_ld();
@@ -116,7 +118,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
         }
     } else if constexpr (EPI == kEpiResid) {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = g; c < BN / 32; c += kEpiGroups) {
             float v[32];
             tmem_ld32(tbase + c * 32, v);
             tmem_wait_ld();
@@ -137,7 +139,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
     } else if constexpr (EPI == kEpiSwiGLU) {
         const int o0 = nb * (BN / 2);
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = g; c < BN / 64; c += kEpiGroups) {
             float g[32], u[32];
             tmem_ld32(tbase + c * 32, g);
             tmem_ld32(tbase + BN / 2 + c * 32, u);
@@ -153,7 +155,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
         const int nq = p.n_q_heads, nkv = p.n_kv_heads;
         const int ps = valid ? __ldg(p.pos + grow) : 0;
 #pragma unroll 1
-        for (int h0 = 0; h0 < BN; h0 += hd) {
+        for (int h0 = g * hd; h0 < BN; h0 += kEpiGroups * hd) {
             const int col0 = n0 + h0;
             const int gh = col0 / hd;
             const bool is_q = gh < nq;
@@ -199,19 +201,30 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                     add_bias32(x2, p.bias, col0 + half + c * 32);
                 }
                 if (nw) {
+                    const float4 *w1 = reinterpret_cast<const float4 *>(nw + c * 32);
+                    const float4 *w2 = reinterpret_cast<const float4 *>(nw + half + c * 32);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        x1[i] = x1[i] * inv * __ldg(nw + c * 32 + i);
-                        x2[i] = x2[i] * inv * __ldg(nw + half + c * 32 + i);
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 a = __ldg(w1 + i), b = __ldg(w2 + i);
+                        x1[4 * i] = x1[4 * i] * inv * a.x; x1[4 * i + 1] = x1[4 * i + 1] * inv * a.y;
+                        x1[4 * i + 2] = x1[4 * i + 2] * inv * a.z; x1[4 * i + 3] = x1[4 * i + 3] * inv * a.w;
+                        x2[4 * i] = x2[4 * i] * inv * b.x; x2[4 * i + 1] = x2[4 * i + 1] * inv * b.y;
+                        x2[4 * i + 2] = x2[4 * i + 2] * inv * b.z; x2[4 * i + 3] = x2[4 * i + 3] * inv * b.w;
                     }
                 }
+                const float4 *c4 = reinterpret_cast<const float4 *>(cs + c * 32);
+                const float4 *s4 = reinterpret_cast<const float4 *>(sn + c * 32);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float cv = __ldg(cs + c * 32 + i);
-                    const float sv = __ldg(sn + c * 32 + i);
-                    const float a = x1[i], b = x2[i];
-                    x1[i] = a * cv - b * sv;
-                    x2[i] = b * cv + a * sv;
+                for (int i = 0; i < 8; ++i) {
+                    const float4 cv = __ldg(c4 + i), sv = __ldg(s4 + i);
+                    const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+                    const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float a = x1[4 * i + u], b = x2[4 * i + u];
+                        x1[4 * i + u] = a * cc[u] - b * ss[u];
+                        x2[4 * i + u] = b * cc[u] + a * ss[u];
+                    }
                 }
                 store_row32(p, grow, col0 + c * 32, x1);
                 store_row32(p, grow, col0 + half + c * 32, x2);
@@ -252,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull_bar[a], 1);
-            mbar_init(&tempty_bar[a], 4);
+            mbar_init(&tempty_bar[a], 4 * kEpiGroups);
         }
         mbar_init(&drain_bar, 1);
         abort_sh = 0;
@@ -363,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // -------------------------------------------------------------- epilogue
         const int q = warp & 3;
+        const int g = (warp - 2) >> 2;
         const int row = q * 32 + lane;
         int lt = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
@@ -373,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int mb = tile / n_blocks, nb = tile % n_blocks;
             const int grow = mb * BM + row;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
-            epilogue_tile<BN, EPI>(p, tbase, grow, grow < p.M, nb);
+            epilogue_tile<BN, EPI>(p, tbase, grow, grow < p.M, nb, g);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[a]);
