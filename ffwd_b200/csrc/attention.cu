@@ -25,7 +25,11 @@ namespace fb {
 namespace {
 
 constexpr int kTile = 128;  // query rows and keys per tile
-constexpr int kAttnThreads = 384;
+// Softmax warps 0-15 (block w = warp / 8, column half hf = (warp / 4) % 2),
+// producer warp 16, MMA warp 17.
+constexpr int kAttnThreads = 576;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
 constexpr int kRingSlots = 3;
 constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
 
@@ -42,7 +46,14 @@ struct AttnCfg {
     static constexpr int OFF_Q = 0;                                  // Q0, Q1
     static constexpr int OFF_RING = 2 * TILE_BYTES;
     static constexpr int OFF_P = OFF_RING + kRingSlots * TILE_BYTES; // P0, P1
-    static constexpr int SMEM = OFF_P + 2 * P_BYTES + 1024;
+    static constexpr int OFF_MISC = OFF_P + 2 * P_BYTES;             // barriers + row exchange
+    static constexpr int MISC_BYTES = 256 + 2 * 2 * kTile * 4;
+    static constexpr int USED = OFF_MISC + MISC_BYTES;
+    // Slack for aligning the dynamic window to 1024 bytes where it fits the
+    // 227 KB limit; for head_dim 128 the window must already be aligned
+    // (checked at run time).
+    static constexpr int PAD = USED + 1024 <= 232448 - 1024 ? 1024 : 0;
+    static constexpr int SMEM = USED + PAD;
     static constexpr int TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D, ..)
 };
 
@@ -60,17 +71,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     using C = AttnCfg<D>;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t q_full;
-    __shared__ __align__(8) uint64_t ring_full[kRingSlots], ring_empty[kRingSlots];
-    __shared__ __align__(8) uint64_t s_full[2], p_full[2], o_final[2];
-    __shared__ __align__(8) uint64_t drain;
-    __shared__ uint32_t tmem_base_sh;
-    __shared__ int abort_sh;
-
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    if (smem - smem_raw > C::PAD) {  // window not aligned and no slack: refuse
+        if (threadIdx.x == 0) set_error(p.err, kErrSmemAlign);
+        return;
+    }
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_MISC);
+    uint64_t &q_full = bars[0];
+    uint64_t *ring_full = bars + 1, *ring_empty = bars + 1 + kRingSlots;
+    uint64_t *s_full = bars + 1 + 2 * kRingSlots, *p_full = s_full + 2, *o_final = s_full + 4;
+    uint64_t &drain = s_full[6];
+    uint32_t &tmem_base_sh = *reinterpret_cast<uint32_t *>(smem + C::OFF_MISC + 192);
+    int &abort_sh = *reinterpret_cast<int *>(smem + C::OFF_MISC + 196);
+    // Row exchange between the two halves of a block: [block][half][row].
+    float(*red)[2][kTile] = reinterpret_cast<float(*)[2][kTile]>(smem + C::OFF_MISC + 256);
 
     const AttnItem item = p.items[blockIdx.x];
     const bool two = item.qt1 >= 0;
@@ -89,15 +106,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         for (int w = 0; w < 2; ++w) {
             mbar_init(&s_full[w], 1);
-            mbar_init(&p_full[w], 4);
+            mbar_init(&p_full[w], 8);
             mbar_init(&o_final[w], 1);
         }
         mbar_init(&drain, 1);
         abort_sh = 0;
+        tmem_base_sh = 0;
         fence_barrier_init();
     }
-    if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
-    if (warp == 1) {
+    if (warp == kProducerWarp && lane == 0) tma_prefetch_desc(&tm);
+    if (warp == kMmaWarp) {
         tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
         tmem_relinquish();
     }
@@ -110,7 +128,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint8_t *sRing = smem + C::OFF_RING;
     uint8_t *sP = smem + C::OFF_P;
 
-    if (warp == 0) {
+    if (warp == kProducerWarp) {
         if (lane == 0) {
             // ------------------------------------------------------------ producer
             int issued = 0;
@@ -145,7 +163,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
             constexpr uint32_t IDESC_S = idesc_f16(128, 128, 1, 1, 0, 0);
@@ -222,9 +240,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    } else {
         // ---------------------------------------------------------------- softmax
-        const int w = (warp - 4) >> 2;  // block 0: warps 4-7, block 1: warps 8-11
+        // Block w's score row r is split between two threads (same lane / quad in
+        // warps 8w + q and 8w + 4 + q): half hf owns keys [64 hf, 64 hf + 64) of every
+        // tile and O columns [hf D/2, (hf + 1) D/2).  Row max and row sum are
+        // combined through shared memory under a named barrier per block.
+        constexpr int HD = D / 2;              // O columns per half
+        constexpr int CW = HD < 32 ? HD : 32;  // TMEM access width for O
+        const int w = warp >> 3;
+        const int hf = (warp >> 2) & 1;
         if (w == 0 || two) {
             const int quad = warp & 3;
             const int r = quad * 32 + lane;
@@ -233,23 +258,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int q = qt * kTile + r;
             const float sl2 = p.scale * 1.4426950408889634f;
             const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-            const uint32_t tS = tmem_base + lane_off + w * 128;
-            const uint32_t tO = tmem_base + lane_off + 256 + w * D;
-            uint8_t *sPw = sP + w * C::P_BYTES;
+            const uint32_t tS = tmem_base + lane_off + w * 128 + hf * 64;
+            const uint32_t tO = tmem_base + lane_off + 256 + w * D + hf * HD;
+            // Keys [64 hf, 64 hf + 64) are exactly P block hf (one 128-byte swizzle row).
+            uint8_t *rowp = sP + w * C::P_BYTES + hf * (kTile * 128) + r * 128;
             float m_used = -INFINITY, l = 0.0f;
             bool ok = true;
+            auto o_scale = [&](float alpha) {
+#pragma unroll 1
+                for (int c = 0; c < HD / CW; ++c) {
+                    if constexpr (CW == 32) {
+                        float o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(tO + c * 32, o);
+                    } else {
+                        float o[16];
+                        tmem_ld16(tO + c * 16, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) o[i] *= alpha;
+                        tmem_st16(tO + c * 16, o);
+                    }
+                }
+                tmem_wait_st();
+            };
             for (int j = 0; j < n_kt; ++j) {
                 if (!mbar_wait(&s_full[w], j & 1, p.err, &abort_sh)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const int k0 = j * kTile;
-                // Tiles wholly inside the sequence and below the diagonal need no mask.
-                const bool masked = k0 + kTile > L || (p.causal && k0 + kTile - 1 > qt * kTile);
+                const int k0 = j * kTile + hf * 64;
+                // Halves wholly inside the sequence and below the diagonal need no mask.
+                const bool masked = k0 + 64 > L || (p.causal && k0 + 63 > qt * kTile);
                 float mx = -INFINITY;
-#pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
                     float v[32];
                     tmem_ld32(tS + c * 32, v);
                     tmem_wait_ld();
@@ -257,85 +304,80 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             const int key = k0 + c * 32 + i;
-                            const bool vis = key < L && (!p.causal || key <= q);
-                            mx = fmaxf(mx, vis ? v[i] : -INFINITY);
+                            if (!(key < L && (!p.causal || key <= q))) v[i] = -INFINITY;
                         }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
                     }
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
                 }
+                red[w][hf][r] = mx;
+                named_bar(1 + w, 256);
+                mx = fmaxf(mx, red[w][hf ^ 1][r]);
+                named_bar(1 + w, 256);  // both halves read before the next write
                 const float m_new = fmaxf(m_used, mx * sl2);
                 // tcgen05.ld/st are warp-collective: the rescale decision is taken per
-                // warp (any row over the threshold), each row by its own factor.
+                // warp (any row over the threshold; both halves of a row see the same
+                // maxima, so they decide alike), each row by its own factor.
                 if (j == 0) {
                     m_used = m_new;
                 } else if (__any_sync(0xffffffffu, m_new > m_used + kRescaleLog2)) {
                     // O_w is stable here: PV_{j-1} completed before S_j was published,
                     // and PV_j waits for this block's P_j.
-                    const float alpha = exp2f(m_used - m_new);
-#pragma unroll 1
-                    for (int c = 0; c < D / 32; ++c) {
-                        float o[32];
-                        tmem_ld32(tO + c * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(tO + c * 32, o);
-                    }
-                    tmem_wait_st();
+                    const float alpha = ex2_approx(m_used - m_new);
+                    o_scale(alpha);
                     l *= alpha;
                     m_used = m_new;
                 }
-                float sum = 0.0f;
-#pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
                     float v[32];
                     tmem_ld32(tS + c * 32, v);
                     tmem_wait_ld();
                     uint32_t pk[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        float p0 = exp2f(fmaf(v[2 * i], sl2, -m_used));
-                        float p1 = exp2f(fmaf(v[2 * i + 1], sl2, -m_used));
+                        float p0 = ex2_approx(fmaf(v[2 * i], sl2, -m_used));
+                        float p1 = ex2_approx(fmaf(v[2 * i + 1], sl2, -m_used));
                         if (masked) {
                             const int key = k0 + c * 32 + 2 * i;
                             if (!(key < L && (!p.causal || key <= q))) p0 = 0.0f;
                             if (!(key + 1 < L && (!p.causal || key + 1 <= q))) p1 = 0.0f;
                         }
-                        __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-                        const float2 pf = __bfloat1622float2(pb);
-                        sum += pf.x + pf.y;
-                        pk[i] = *reinterpret_cast<uint32_t *>(&pb);
+                        l += p0 + p1;
+                        pk[i] = pack_bf16x2(p0, p1);
                     }
-                    // Keys [32c, 32c + 32) -> block c/2, 16-byte chunks 4(c%2) .. +3.
-                    uint8_t *rowp = sPw + (c >> 1) * (kTile * 128) + r * 128;
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int chunk = (c & 1) * 4 + u;
+                        const int chunk = c * 4 + u;
                         *reinterpret_cast<uint4 *>(rowp + ((chunk ^ (r & 7)) * 16)) =
                             make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
                     }
                 }
-                l += sum;
                 tc_fence_before();
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[w]);
             }
+            // Combine the halves' row sums (every thread of the block reaches this).
+            red[w][hf][r] = l;
+            named_bar(1 + w, 256);
+            l += red[w][hf ^ 1][r];
             if (ok && mbar_wait(&o_final[w], 0, p.err, &abort_sh)) {
                 tc_fence_after();
                 const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-                __nv_bfloat16 *orow = p.out + (size_t)(seq0 + q) * p.ldo + h * D;
+                __nv_bfloat16 *orow = p.out + (size_t)(seq0 + q) * p.ldo + h * D + hf * HD;
 #pragma unroll 1
-                for (int c = 0; c < D / 32; ++c) {
-                    float o[32];
-                    tmem_ld32(tO + c * 32, o);
+                for (int c = 0; c < HD / CW; ++c) {
+                    float o[CW];
+                    if constexpr (CW == 32)
+                        tmem_ld32(tO + c * 32, o);
+                    else
+                        tmem_ld16(tO + c * 16, o);
                     tmem_wait_ld();
                     if (q < L) {
-                        uint4 *op = reinterpret_cast<uint4 *>(orow + c * 32);
+                        uint4 *op = reinterpret_cast<uint4 *>(orow + c * CW);
 #pragma unroll
-                        for (int u = 0; u < 4; ++u)
+                        for (int u = 0; u < CW / 8; ++u)
                             op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
                                                pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
                                                pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
@@ -348,7 +390,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
