@@ -25,11 +25,13 @@ namespace fb {
 namespace {
 
 constexpr int kTile = 128;  // query rows and keys per tile
-// Softmax warps 0-15 (block w = warp / 8, column half hf = (warp / 4) % 2),
-// producer warp 16, MMA warp 17.
-constexpr int kAttnThreads = 576;
-constexpr int kProducerWarp = 16;
-constexpr int kMmaWarp = 17;
+// Warpgroup 0 (warps 0-3): softmax of block 0; warpgroup 1 (warps 4-7): softmax
+// of block 1; warp 8: producer; warp 9: MMA issuer (warps 10-11 only pad the CTA
+// to three warpgroups).  384 threads leave 168 registers per thread, enough for
+// a softmax thread to hold its whole 128-score row.
+constexpr int kAttnThreads = 384;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr int kRingSlots = 3;
 constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
 
@@ -106,7 +108,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         for (int w = 0; w < 2; ++w) {
             mbar_init(&s_full[w], 1);
-            mbar_init(&p_full[w], 8);
+            mbar_init(&p_full[w], 4);
             mbar_init(&o_final[w], 1);
         }
         mbar_init(&drain, 1);
@@ -240,16 +242,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp < 8) {
         // ---------------------------------------------------------------- softmax
-        // Block w's score row r is split between two threads (same lane / quad in
-        // warps 8w + q and 8w + 4 + q): half hf owns keys [64 hf, 64 hf + 64) of every
-        // tile and O columns [hf D/2, (hf + 1) D/2).  Row max and row sum are
-        // combined through shared memory under a named barrier per block.
-        constexpr int HD = D / 2;              // O columns per half
-        constexpr int CW = HD < 32 ? HD : 32;  // TMEM access width for O
-        const int w = warp >> 3;
-        const int hf = (warp >> 2) & 1;
+        // One thread per query row: the row's 128 scores of a tile are read from
+        // TMEM once (four loads in flight) and kept in registers.
+        const int w = warp >> 2;
         if (w == 0 || two) {
             const int quad = warp & 3;
             const int r = quad * 32 + lane;
@@ -258,126 +255,99 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int q = qt * kTile + r;
             const float sl2 = p.scale * 1.4426950408889634f;
             const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-            const uint32_t tS = tmem_base + lane_off + w * 128 + hf * 64;
-            const uint32_t tO = tmem_base + lane_off + 256 + w * D + hf * HD;
-            // Keys [64 hf, 64 hf + 64) are exactly P block hf (one 128-byte swizzle row).
-            uint8_t *rowp = sP + w * C::P_BYTES + hf * (kTile * 128) + r * 128;
+            const uint32_t tS = tmem_base + lane_off + w * 128;
+            const uint32_t tO = tmem_base + lane_off + 256 + w * D;
+            uint8_t *rowp0 = sP + w * C::P_BYTES + r * 128;
             float m_used = -INFINITY, l = 0.0f;
             bool ok = true;
-            auto o_scale = [&](float alpha) {
-#pragma unroll 1
-                for (int c = 0; c < HD / CW; ++c) {
-                    if constexpr (CW == 32) {
-                        float o[32];
-                        tmem_ld32(tO + c * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(tO + c * 32, o);
-                    } else {
-                        float o[16];
-                        tmem_ld16(tO + c * 16, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) o[i] *= alpha;
-                        tmem_st16(tO + c * 16, o);
-                    }
-                }
-                tmem_wait_st();
-            };
             for (int j = 0; j < n_kt; ++j) {
                 if (!mbar_wait(&s_full[w], j & 1, p.err, &abort_sh)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const int k0 = j * kTile + hf * 64;
-                // Halves wholly inside the sequence and below the diagonal need no mask.
-                const bool masked = k0 + 64 > L || (p.causal && k0 + 63 > qt * kTile);
-                float mx = -INFINITY;
+                float v0[32], v1[32], v2[32], v3[32];
+                tmem_ld32(tS, v0);
+                tmem_ld32(tS + 32, v1);
+                tmem_ld32(tS + 64, v2);
+                tmem_ld32(tS + 96, v3);
+                tmem_wait_ld();
+#define V(i) ((i) < 32 ? v0[(i)] : (i) < 64 ? v1[(i) - 32] : (i) < 96 ? v2[(i) - 64] : v3[(i) - 96])
+                const int k0 = j * kTile;
+                // Tiles wholly inside the sequence and below the diagonal need no mask.
+                if (k0 + kTile > L || (p.causal && k0 + kTile - 1 > qt * kTile)) {
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    float v[32];
-                    tmem_ld32(tS + c * 32, v);
-                    tmem_wait_ld();
-                    if (masked) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int key = k0 + c * 32 + i;
-                            if (!(key < L && (!p.causal || key <= q))) v[i] = -INFINITY;
-                        }
+                    for (int i = 0; i < 128; ++i) {
+                        const int key = k0 + i;
+                        if (!(key < L && (!p.causal || key <= q))) V(i) = -INFINITY;
                     }
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
                 }
-                red[w][hf][r] = mx;
-                named_bar(1 + w, 256);
-                mx = fmaxf(mx, red[w][hf ^ 1][r]);
-                named_bar(1 + w, 256);  // both halves read before the next write
+                float mxa[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mxa[i] = V(i);
+#pragma unroll
+                for (int i = 8; i < 128; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], V(i));
+                const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
                 const float m_new = fmaxf(m_used, mx * sl2);
                 // tcgen05.ld/st are warp-collective: the rescale decision is taken per
-                // warp (any row over the threshold; both halves of a row see the same
-                // maxima, so they decide alike), each row by its own factor.
+                // warp (any row over the threshold), each row by its own factor.
                 if (j == 0) {
                     m_used = m_new;
                 } else if (__any_sync(0xffffffffu, m_new > m_used + kRescaleLog2)) {
                     // O_w is stable here: PV_{j-1} completed before S_j was published,
                     // and PV_j waits for this block's P_j.
                     const float alpha = ex2_approx(m_used - m_new);
-                    o_scale(alpha);
+#pragma unroll 1
+                    for (int c = 0; c < D / 32; ++c) {
+                        float o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(tO + c * 32, o);
+                    }
+                    tmem_wait_st();
                     l *= alpha;
                     m_used = m_new;
                 }
+                float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    float v[32];
-                    tmem_ld32(tS + c * 32, v);
-                    tmem_wait_ld();
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float p0 = ex2_approx(fmaf(v[2 * i], sl2, -m_used));
-                        float p1 = ex2_approx(fmaf(v[2 * i + 1], sl2, -m_used));
-                        if (masked) {
-                            const int key = k0 + c * 32 + 2 * i;
-                            if (!(key < L && (!p.causal || key <= q))) p0 = 0.0f;
-                            if (!(key + 1 < L && (!p.causal || key + 1 <= q))) p1 = 0.0f;
-                        }
-                        l += p0 + p1;
-                        pk[i] = pack_bf16x2(p0, p1);
-                    }
+                for (int ch = 0; ch < 16; ++ch) {  // 16-byte chunk = 8 keys
+                    uint32_t pk[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int chunk = c * 4 + u;
-                        *reinterpret_cast<uint4 *>(rowp + ((chunk ^ (r & 7)) * 16)) =
-                            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+                        const float p0 = ex2_approx(fmaf(V(8 * ch + 2 * u), sl2, -m_used));
+                        const float p1 = ex2_approx(fmaf(V(8 * ch + 2 * u + 1), sl2, -m_used));
+                        la[u] += p0 + p1;
+                        pk[u] = pack_bf16x2(p0, p1);
                     }
+                    // Keys [8 ch, 8 ch + 8) -> block ch / 8, swizzled chunk ch % 8.
+                    *reinterpret_cast<uint4 *>(rowp0 + (ch >> 3) * (kTile * 128) +
+                                               (((ch & 7) ^ (r & 7)) * 16)) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    asm volatile("" ::: "memory");  // keep the exp / pack / store per chunk
                 }
+#undef V
+                l += (la[0] + la[1]) + (la[2] + la[3]);
                 tc_fence_before();
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[w]);
             }
-            // Combine the halves' row sums (every thread of the block reaches this).
-            red[w][hf][r] = l;
-            named_bar(1 + w, 256);
-            l += red[w][hf ^ 1][r];
             if (ok && mbar_wait(&o_final[w], 0, p.err, &abort_sh)) {
                 tc_fence_after();
                 const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-                __nv_bfloat16 *orow = p.out + (size_t)(seq0 + q) * p.ldo + h * D + hf * HD;
+                __nv_bfloat16 *orow = p.out + (size_t)(seq0 + q) * p.ldo + h * D;
 #pragma unroll 1
-                for (int c = 0; c < HD / CW; ++c) {
-                    float o[CW];
-                    if constexpr (CW == 32)
-                        tmem_ld32(tO + c * 32, o);
-                    else
-                        tmem_ld16(tO + c * 16, o);
+                for (int c = 0; c < D / 32; ++c) {
+                    float o[32];
+                    tmem_ld32(tO + c * 32, o);
                     tmem_wait_ld();
                     if (q < L) {
-                        uint4 *op = reinterpret_cast<uint4 *>(orow + c * CW);
+                        uint4 *op = reinterpret_cast<uint4 *>(orow + c * 32);
 #pragma unroll
-                        for (int u = 0; u < CW / 8; ++u)
+                        for (int u = 0; u < 4; ++u)
                             op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
                                                pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
                                                pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
