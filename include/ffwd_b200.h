@@ -169,7 +169,7 @@ FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const i
  * 32 MiB arena of device memory reserved, on every GPU that loads the library,
  * until the process exits.  Requests whose buffers do not fit the arena (for
  * example more than about 1300 tokens for a Qwen3-0.6B-shaped model), more
- * than 4096 sequences or 8192 attention tiles are rejected with -1 and a
+ * than 4096 sequences or 8192 attention work items are rejected with -1 and a
  * message.  The first call on a device resolves the arena's device address
  * with that device current; make that first call before any stream capture.
  * All calls share the one arena and it keeps the last call's contents, so
