@@ -120,6 +120,7 @@ struct Mat {
     __nv_bfloat16 *lo = nullptr;  // 3-pass mode only
     int rows = 0, cols = 0, bn = 128;
     CUtensorMap map_hi, map_lo;
+    CUtensorMap map_half;  // 128-row box over hi, for the two-SM kernel (bn == 256)
 };
 
 struct LayerW {
@@ -294,6 +295,9 @@ int upload_mat(Device &D, const HostMat &hm, int bn, Mat &m) {
     if (dev_alloc(D, &m.hi, hm.hi.size())) return -1;
     CK(cudaMemcpy(m.hi, hm.hi.data(), hm.hi.size() * 2, cudaMemcpyHostToDevice));
     if (make_map(&m.map_hi, m.hi, m.rows, m.cols, bn, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
+    if (bn == 256 &&
+        make_map(&m.map_half, m.hi, m.rows, m.cols, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
     if (!hm.lo.empty()) {
         if (dev_alloc(D, &m.lo, hm.lo.size())) return -1;
         CK(cudaMemcpy(m.lo, hm.lo.data(), hm.lo.size() * 2, cudaMemcpyHostToDevice));
@@ -576,11 +580,25 @@ __global__ void positions_kernel(const int *offsets, int pos_offset, int *pos) {
     for (int t = s + threadIdx.x; t < e; t += blockDim.x) pos[t] = pos_offset + (t - s);
 }
 
+// Single-pass GEMMs with 256-wide tiles run on the two-SM kernel unless
+// FFWD_B200_GEMM_2SM=0 (A/B comparisons).
+bool use_gemm2() {
+    static const bool on = [] {
+        const char *e = getenv("FFWD_B200_GEMM_2SM");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 int gemm(Device &D, int prec, const CUtensorMap *a, const CUtensorMap *a_lo, const Mat &w,
          GemmParams &p) {
     p.N = w.rows;
     p.K = w.cols;
     const int passes = prec == 0 ? 1 : prec;
+    if (passes == 1 && w.bn == 256 && use_gemm2()) {
+        LAUNCH(gemm2_launch(a, &w.map_half, p, D.num_sms, D.stream));
+        return 0;
+    }
     LAUNCH(gemm_launch(a, passes >= 2 ? a_lo : nullptr, &w.map_hi, passes == 3 ? &w.map_lo : nullptr,
                        w.bn, passes, p, D.num_sms, D.stream));
     return 0;
@@ -1262,8 +1280,14 @@ FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const voi
     p.out_mode = kOutF32;
     p.out = y;
     p.ldo = N;
-    LAUNCH(gemm_launch(&ma, x_lo ? &mal : nullptr, &mb, w_lo ? &mbl : nullptr, bn, passes, p, sms,
-                       0));
+    if (passes == 1 && bn == 256 && use_gemm2()) {
+        CUtensorMap mh;
+        if (make_map(&mh, w, N, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
+        LAUNCH(gemm2_launch(&ma, &mh, p, sms, 0));
+    } else {
+        LAUNCH(gemm_launch(&ma, x_lo ? &mal : nullptr, &mb, w_lo ? &mbl : nullptr, bn, passes, p,
+                           sms, 0));
+    }
     CK(cudaDeviceSynchronize());
     return 0;
 }

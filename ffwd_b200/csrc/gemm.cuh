@@ -60,4 +60,10 @@ int gemm_launch(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap
                 const CUtensorMap *b_lo, int bn, int passes, const GemmParams &p, int num_sms,
                 cudaStream_t stream);
 
+// Two-SM variant (cluster of two CTAs, tcgen05.mma.cta_group::2, M = 256 per
+// pair) for single-pass bf16 with N a multiple of 256.  `b_half` maps W with a
+// box of 128 rows x 64 columns (each CTA loads its half of a 256-row tile).
+int gemm2_launch(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p, int num_sms,
+                 cudaStream_t stream);
+
 }  // namespace fb

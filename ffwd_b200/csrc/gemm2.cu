@@ -1,0 +1,286 @@
+// Two-SM tcgen05 projection GEMM (cta_group::2) with the fused epilogues of
+// gemm_epi.cuh, for single-pass bf16 projections with N a multiple of 256.
+//
+// A cluster of two CTAs (two SMs) computes a 256 x 256 output tile: CTA r holds
+// rows [128 r, 128 r + 128) of the X tile and rows [128 r, 128 r + 128) of the
+// 256-row W tile in its own shared memory; the leader CTA (rank 0) issues
+// tcgen05.mma.cta_group::2 with M = 256, which reads A from each CTA and the two
+// W halves from both, and accumulates each CTA's 128 output rows in that CTA's
+// TMEM.  Compared with the one-SM kernel every SM stages half as much W per
+// FLOP.  Roles per CTA (320 threads):
+//   warp 0      TMA producer for this CTA's halves; the transaction bytes of both
+//               CTAs complete on the leader's stage barrier.
+//   warp 1      TMEM allocation (both CTAs); on the leader, the MMA issuer.  Its
+//               commits arrive on the barriers of both CTAs.
+//   warps 2-9   epilogue of this CTA's 128 rows (two warpgroups split columns);
+//               they release an accumulator on the leader's barrier.
+// No TMA load here uses cluster multicast.
+#include "gemm.cuh"
+#include "gemm_epi.cuh"
+#include "ptx.cuh"
+
+#include <cuda_runtime.h>
+
+namespace fb {
+namespace {
+
+constexpr int BM = 128;  // rows per CTA
+constexpr int BN = 256;  // output columns per tile
+constexpr int BK = 64;
+using epi::kEpiGroups;
+using epi::epilogue_tile;
+constexpr int kThreads = 64 + 128 * kEpiGroups;
+constexpr int A_BYTES = BM * BK * 2;         // this CTA's X rows
+constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int STAGES = 6;
+constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // clears the CTA-rank bit: leader's copy
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+
+// Tile load into this CTA's shared memory, transaction bytes counted on the
+// barrier at `bar_leader` (leader CTA).
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m, uint32_t bar_leader,
+                                                 int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_leader), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs once the issued MMAs complete.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+    const uint16_t mask = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_u32(bar)),
+        "h"(mask)
+        : "memory");
+}
+
+// Arrive on the leader CTA's copy of `bar`.
+__device__ __forceinline__ void arrive_leader(uint64_t *bar) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(smem_u32(bar)));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote)
+                 : "memory");
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t tfull_bar[2];
+    __shared__ __align__(8) uint64_t tempty_bar[2];
+    __shared__ __align__(8) uint64_t drain_bar;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+    const int m_blocks = (p.M + 2 * BM - 1) / (2 * BM);
+    const int n_blocks = p.N / BN;
+    const int num_tiles = m_blocks * n_blocks;
+    const int k_blocks = p.K / BK;
+    const int pair = blockIdx.x >> 1;
+    const int n_pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 2 * 4 * kEpiGroups);
+        }
+        mbar_init(&drain_bar, 1);
+        abort_sh = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&tmem_base_sh)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers initialised before any remote use
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------------------------------------------------- producer
+            const uint64_t pol_w = policy_evict_last();
+            (void)pol_w;
+            int it = 0;
+            bool ok = true;
+            for (int tile = pair; ok && tile < num_tiles; tile += n_pairs) {
+                const int mb = tile / n_blocks, nb = tile % n_blocks;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, &abort_sh)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = smem + s * STAGE_BYTES;
+                    if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * STAGE_BYTES);
+                    const uint32_t bar = smem_u32(&full_bar[s]) & kPeerMask;
+                    tma_load_2d_pair(st, &tmA, bar, kb * BK, mb * 2 * BM + rank * BM);
+                    tma_load_2d_pair(st + A_BYTES, &tmB, bar, kb * BK, nb * BN + rank * (BN / 2));
+                    ++it;
+                }
+            }
+            if (!ok && leader) {
+                for (int j = it - STAGES < 0 ? 0 : it - STAGES; j < it; ++j)
+                    mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, nullptr, nullptr);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            // ---------------------------------------------------------- MMA issuer
+            constexpr uint32_t IDESC = idesc_f16(2 * BM, BN, 1, 1, 0, 0);
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = pair; ok && tile < num_tiles; tile += n_pairs, ++lt) {
+                const int a = lt & 1;
+                const uint32_t aph = (lt >> 1) & 1;
+                if (!mbar_wait(&tempty_bar[a], aph ^ 1, p.err, &abort_sh)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + a * BN;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(&full_bar[s], ph, p.err, &abort_sh)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+                    const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_pair(d, smem_desc(sa + kk * 32, 16, 1024, kLayoutSW128),
+                                  smem_desc(sb + kk * 32, 16, 1024, kLayoutSW128), IDESC,
+                                  (kb | kk) != 0);
+                    umma_commit_pair(&empty_bar[s]);
+                    ++it;
+                }
+                if (!ok) break;
+                umma_commit_pair(&tfull_bar[a]);
+            }
+            if (!ok) {
+                asm volatile(
+                    "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                        smem_u32(&drain_bar))
+                    : "memory");
+                mbar_wait(&drain_bar, 0, nullptr, nullptr);
+            }
+        }
+        __syncwarp();
+    } else {
+        // -------------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int g = (warp - 2) >> 2;
+        const int row = q * 32 + lane;
+        int lt = 0;
+        for (int tile = pair; tile < num_tiles; tile += n_pairs, ++lt) {
+            const int a = lt & 1;
+            const uint32_t aph = (lt >> 1) & 1;
+            if (!mbar_wait(&tfull_bar[a], aph, p.err, &abort_sh)) break;
+            tc_fence_after();
+            const int mb = tile / n_blocks, nb = tile % n_blocks;
+            const int grow = mb * 2 * BM + rank * BM + row;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
+            epilogue_tile<BN, EPI>(p, tbase, grow, grow < p.M, nb, g);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) arrive_leader(&tempty_bar[a]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer may still touch its barriers or smem
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+template <int EPI>
+int launch2(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p, int num_sms,
+            cudaStream_t stream) {
+    auto kern = gemm2_kernel<EPI>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / BN);
+    int grid = 2 * tiles;
+    const int cap = num_sms & ~1;
+    if (grid > cap) grid = cap;
+    kern<<<grid, kThreads, SMEM, stream>>>(*a, *b_half, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int gemm2_launch(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p, int num_sms,
+                 cudaStream_t stream) {
+    if (p.M <= 0 || p.K % BK != 0 || p.N % BN != 0) return cudaErrorInvalidValue;
+    if (p.epi == kEpiQKRope && (p.head_dim % 64 != 0 || BN % p.head_dim != 0))
+        return cudaErrorInvalidValue;
+    switch (p.epi) {
+    case kEpiStore: return launch2<kEpiStore>(a, b_half, p, num_sms, stream);
+    case kEpiGelu: return launch2<kEpiGelu>(a, b_half, p, num_sms, stream);
+    case kEpiResid: return launch2<kEpiResid>(a, b_half, p, num_sms, stream);
+    case kEpiSwiGLU: return launch2<kEpiSwiGLU>(a, b_half, p, num_sms, stream);
+    case kEpiQKRope: return launch2<kEpiQKRope>(a, b_half, p, num_sms, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace fb

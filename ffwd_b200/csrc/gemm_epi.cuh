@@ -1,0 +1,212 @@
+// Fused GEMM epilogues shared by the 1-SM and 2-SM tcgen05 GEMM kernels:
+// each epilogue thread owns one accumulator row (TMEM lane) of a 128-row tile
+// and processes its columns 32 at a time; warpgroup g of kEpiGroups takes every
+// kEpiGroups-th unit of the tile.
+#pragma once
+
+#include "gemm.cuh"
+#include "ptx.cuh"
+
+namespace fb {
+namespace epi {
+
+constexpr int kEpiGroups = 2;
+
+__device__ __forceinline__ float gelu_erf(float x) {
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    float inner = 0.79788456080286536f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ void add_bias32(float (&v)[32], const float *bias, int col) {
+    const float4 *b4 = reinterpret_cast<const float4 *>(bias + col);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float4 b = __ldg(b4 + i);
+        v[4 * i + 0] += b.x;
+        v[4 * i + 1] += b.y;
+        v[4 * i + 2] += b.z;
+        v[4 * i + 3] += b.w;
+    }
+}
+
+// Store 32 consecutive values of one row in the requested encoding.
+__device__ __forceinline__ void store_row32(const GemmParams &p, int row, int col,
+                                            const float (&v)[32]) {
+    const size_t off = (size_t)row * p.ldo + col;
+    if (p.out_mode == kOutF32) {
+        float4 *o = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        return;
+    }
+    uint32_t hi[16];
+    uint32_t lo[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * i]);
+        __nv_bfloat16 h1 = __float2bfloat16_rn(v[2 * i + 1]);
+        __nv_bfloat162 hh(h0, h1);
+        hi[i] = *reinterpret_cast<uint32_t *>(&hh);
+        if (p.out_mode == kOutSplit)
+            lo[i] = pack_bf16x2(v[2 * i] - __bfloat162float(h0), v[2 * i + 1] - __bfloat162float(h1));
+    }
+    uint4 *o = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.out) + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = make_uint4(hi[4 * i], hi[4 * i + 1], hi[4 * i + 2], hi[4 * i + 3]);
+    if (p.out_mode == kOutSplit) {
+        uint4 *ol = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.out_lo) + off);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            ol[i] = make_uint4(lo[4 * i], lo[4 * i + 1], lo[4 * i + 2], lo[4 * i + 3]);
+    }
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbase, int grow,
+                                              bool valid, int nb, int g) {
+    // Warpgroup g of kEpiGroups handles every kEpiGroups-th unit of the tile.
+    const int n0 = nb * BN;
+    if constexpr (EPI == kEpiStore || EPI == kEpiGelu) {
+#pragma unroll 1
+        for (int c = g; c < BN / 32; c += kEpiGroups) {
+            float v[32];
+            tmem_ld32(tbase + c * 32, v);
+            tmem_wait_ld();
+            if (!valid) continue;
+            const int col = n0 + c * 32;
+            if (p.bias) add_bias32(v, p.bias, col);
+            if constexpr (EPI == kEpiGelu) {
+                if (p.gelu_tanh) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+                }
+            }
+            store_row32(p, grow, col, v);
+        }
+    } else if constexpr (EPI == kEpiResid) {
+#pragma unroll 1
+        for (int c = g; c < BN / 32; c += kEpiGroups) {
+            float v[32];
+            tmem_ld32(tbase + c * 32, v);
+            tmem_wait_ld();
+            if (!valid) continue;
+            const int col = n0 + c * 32;
+            if (p.bias) add_bias32(v, p.bias, col);
+            float4 *r = reinterpret_cast<float4 *>(p.resid + (size_t)grow * p.ldr + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float4 x = r[i];
+                x.x += v[4 * i];
+                x.y += v[4 * i + 1];
+                x.z += v[4 * i + 2];
+                x.w += v[4 * i + 3];
+                r[i] = x;
+            }
+        }
+    } else if constexpr (EPI == kEpiSwiGLU) {
+        const int o0 = nb * (BN / 2);
+#pragma unroll 1
+        for (int c = g; c < BN / 64; c += kEpiGroups) {
+            float g[32], u[32];
+            tmem_ld32(tbase + c * 32, g);
+            tmem_ld32(tbase + BN / 2 + c * 32, u);
+            tmem_wait_ld();
+            if (!valid) continue;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) g[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
+            store_row32(p, grow, o0 + c * 32, g);
+        }
+    } else if constexpr (EPI == kEpiQKRope) {
+        const int hd = p.head_dim;
+        const int half = hd / 2;
+        const int nq = p.n_q_heads, nkv = p.n_kv_heads;
+        const int ps = valid ? __ldg(p.pos + grow) : 0;
+#pragma unroll 1
+        for (int h0 = g * hd; h0 < BN; h0 += kEpiGroups * hd) {
+            const int col0 = n0 + h0;
+            const int gh = col0 / hd;
+            const bool is_q = gh < nq;
+            const bool is_k = !is_q && gh < nq + nkv;
+            if (!is_q && !is_k) {
+#pragma unroll 1
+                for (int c = 0; c < hd / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(tbase + h0 + c * 32, v);
+                    tmem_wait_ld();
+                    if (!valid) continue;
+                    if (p.bias) add_bias32(v, p.bias, col0 + c * 32);
+                    store_row32(p, grow, col0 + c * 32, v);
+                }
+                continue;
+            }
+            const float *nw = is_q ? p.q_norm : p.k_norm;
+            float inv = 1.0f;
+            if (nw) {
+                float ss = 0.0f;
+#pragma unroll 1
+                for (int c = 0; c < hd / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(tbase + h0 + c * 32, v);
+                    tmem_wait_ld();
+                    if (p.bias && valid) add_bias32(v, p.bias, col0 + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+                }
+                inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
+            }
+            const float *cs = p.rope_cos + (size_t)ps * half;
+            const float *sn = p.rope_sin + (size_t)ps * half;
+#pragma unroll 1
+            for (int c = 0; c < half / 32; ++c) {
+                float x1[32], x2[32];
+                tmem_ld32(tbase + h0 + c * 32, x1);
+                tmem_ld32(tbase + h0 + half + c * 32, x2);
+                tmem_wait_ld();
+                if (!valid) continue;
+                if (p.bias) {
+                    add_bias32(x1, p.bias, col0 + c * 32);
+                    add_bias32(x2, p.bias, col0 + half + c * 32);
+                }
+                if (nw) {
+                    const float4 *w1 = reinterpret_cast<const float4 *>(nw + c * 32);
+                    const float4 *w2 = reinterpret_cast<const float4 *>(nw + half + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 a = __ldg(w1 + i), b = __ldg(w2 + i);
+                        x1[4 * i] = x1[4 * i] * inv * a.x; x1[4 * i + 1] = x1[4 * i + 1] * inv * a.y;
+                        x1[4 * i + 2] = x1[4 * i + 2] * inv * a.z; x1[4 * i + 3] = x1[4 * i + 3] * inv * a.w;
+                        x2[4 * i] = x2[4 * i] * inv * b.x; x2[4 * i + 1] = x2[4 * i + 1] * inv * b.y;
+                        x2[4 * i + 2] = x2[4 * i + 2] * inv * b.z; x2[4 * i + 3] = x2[4 * i + 3] * inv * b.w;
+                    }
+                }
+                const float4 *c4 = reinterpret_cast<const float4 *>(cs + c * 32);
+                const float4 *s4 = reinterpret_cast<const float4 *>(sn + c * 32);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 cv = __ldg(c4 + i), sv = __ldg(s4 + i);
+                    const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+                    const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float a = x1[4 * i + u], b = x2[4 * i + u];
+                        x1[4 * i + u] = a * cc[u] - b * ss[u];
+                        x2[4 * i + u] = b * cc[u] + a * ss[u];
+                    }
+                }
+                store_row32(p, grow, col0 + c * 32, x1);
+                store_row32(p, grow, col0 + half + c * 32, x2);
+            }
+        }
+    }
+}
+
+}  // namespace epi
+}  // namespace fb
