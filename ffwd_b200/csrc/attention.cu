@@ -178,25 +178,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             auto wait_slot = [&](int i) -> bool {
                 return mbar_wait(&ring_full[i % kRingSlots], (i / kRingSlots) & 1, p.err, &abort_sh);
             };
+            // Descriptors are linear in the start address (16-byte units in the low
+            // bits), so each operand's descriptor is built once and offset per MMA.
+            const uint64_t dQ = kmajor_desc<D>(aQ, 0);
+            const uint64_t dRingK = kmajor_desc<D>(aRing, 0);
+            const uint64_t dRingV = smem_desc(aRing, C::BOX_BYTES, C::SBO, C::LAYOUT);
+            const uint64_t dP = smem_desc(aP, 16, 1024, kLayoutSW128);
+            auto koff = [](int kk) -> uint64_t {  // K-major k-step offset (16-byte units)
+                const int e = kk * 16;
+                return (uint64_t)(((e / C::BOXC) * C::BOX_BYTES + (e % C::BOXC) * 2) >> 4);
+            };
             auto issue_s = [&](int w, int j) {
-                const uint32_t aK = aRing + slot_of(2 * j) * C::TILE_BYTES;
-                const uint32_t aQw = aQ + w * C::TILE_BYTES;
+                const uint64_t dK = dRingK + (uint64_t)((slot_of(2 * j) * C::TILE_BYTES) >> 4);
+                const uint64_t dQw = dQ + (uint64_t)((w * C::TILE_BYTES) >> 4);
+                const uint32_t d = tmem_base + w * 128;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(tmem_base + w * 128, kmajor_desc<D>(aQw, kk), kmajor_desc<D>(aK, kk),
-                             IDESC_S, kk != 0);
+                    umma_f16(d, dQw + koff(kk), dK + koff(kk), IDESC_S, kk != 0);
             };
             auto issue_pv = [&](int w, int j) {
-                const uint32_t aV = aRing + slot_of(2 * j + 1) * C::TILE_BYTES;
-                const uint32_t aPw = aP + w * C::P_BYTES;
+                const uint64_t dV = dRingV + (uint64_t)((slot_of(2 * j + 1) * C::TILE_BYTES) >> 4);
+                const uint64_t dPw = dP + (uint64_t)((w * C::P_BYTES) >> 4);
+                const uint32_t d = tmem_base + 256 + w * D;
 #pragma unroll
-                for (int kk = 0; kk < kTile / 16; ++kk) {
-                    const uint64_t pd = smem_desc(aPw + (kk / 4) * (kTile * 128) + (kk % 4) * 32, 16,
-                                                  1024, kLayoutSW128);
-                    const uint64_t vd = smem_desc(aV + kk * 16 * C::ROWB, C::BOX_BYTES, C::SBO,
-                                                  C::LAYOUT);
-                    umma_f16(tmem_base + 256 + w * D, pd, vd, IDESC_O, (j | kk) != 0);
-                }
+                for (int kk = 0; kk < kTile / 16; ++kk)
+                    umma_f16(d, dPw + (uint64_t)(((kk / 4) * (kTile * 128) + (kk % 4) * 32) >> 4),
+                             dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O, (j | kk) != 0);
             };
             bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh) && wait_slot(0);
             if (ok) {

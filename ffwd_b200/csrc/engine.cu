@@ -8,7 +8,7 @@
 // cuda_forward_batch 4975-5100; BERT forward cuda_forward_batch_bert
 // 4634-4973; encode entry points 5102-5225.  The reference drives one GPU; the
 // device set and the LPT sharder below have no counterpart there.
-#include "../../include/ffwd_b200.h"
+#include "ffwd_b200.h"
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "loader.h"

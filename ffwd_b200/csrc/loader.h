@@ -5,7 +5,7 @@
 // libffwd/safetensors.c:351-467).
 #pragma once
 
-#include "../../include/ffwd_b200.h"
+#include "ffwd_b200.h"
 
 #include <cstdint>
 #include <map>

@@ -8,6 +8,10 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#ifndef FFWD_B200_SPIN_PROBE
+#define FFWD_B200_SPIN_PROBE mbar_try_wait
+#endif
+
 namespace fb {
 
 // ----------------------------------------------------------------- error codes
@@ -80,6 +84,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
     return ok != 0;
 }
 
+// Non-suspending probe of phase `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on phase `parity`.  `abort` (shared flag) lets a role give up
 // early once another role of the same CTA has already timed out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err,
@@ -88,7 +105,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
-        if (mbar_try_wait(a, parity)) return true;
+        // Poll without touching the (slow) global timer most of the time.
+#pragma unroll 1
+        for (int i = 0; i < 128; ++i)
+            if (FFWD_B200_SPIN_PROBE(a, parity)) return true;
         if (abort && *abort) return false;
         if (globaltimer() - t0 > kWaitLimitNs) {
             set_error(err, kErrWaitTimeout);
