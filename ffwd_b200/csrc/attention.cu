@@ -17,6 +17,7 @@
 // Masking follows the packed layout: key k of sequence b is visible to query q
 // iff k < len(b) and (bidirectional or k <= q).
 #include "attention.cuh"
+#include "launch_util.cuh"
 #include "ptx.cuh"
 
 #include <algorithm>
@@ -333,7 +334,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     *reinterpret_cast<uint4 *>(rowp0 + (ch >> 3) * (kTile * 128) +
                                                (((ch & 7) ^ (r & 7)) * 16)) =
                         make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    asm volatile("" ::: "memory");  // keep the exp / pack / store per chunk
+                    // Bound the live range: exp / pack / store 32 keys at a time.
+                    if ((ch & 3) == 3) asm volatile("" ::: "memory");
                 }
 #undef V
                 l += (la[0] + la[1]) + (la[2] + la[3]);
@@ -468,20 +470,17 @@ int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStr
     cudaError_t e;
     switch (p.head_dim) {
     case 32:
-        e = cudaFuncSetAttribute(attn_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 AttnCfg<32>::SMEM);
+        e = set_smem_once<attn_tc_kernel<32>>(AttnCfg<32>::SMEM);
         if (e != cudaSuccess) return e;
         attn_tc_kernel<32><<<grid, kAttnThreads, AttnCfg<32>::SMEM, stream>>>(*qkv_map, p);
         break;
     case 64:
-        e = cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 AttnCfg<64>::SMEM);
+        e = set_smem_once<attn_tc_kernel<64>>(AttnCfg<64>::SMEM);
         if (e != cudaSuccess) return e;
         attn_tc_kernel<64><<<grid, kAttnThreads, AttnCfg<64>::SMEM, stream>>>(*qkv_map, p);
         break;
     case 128:
-        e = cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 AttnCfg<128>::SMEM);
+        e = set_smem_once<attn_tc_kernel<128>>(AttnCfg<128>::SMEM);
         if (e != cudaSuccess) return e;
         attn_tc_kernel<128><<<grid, kAttnThreads, AttnCfg<128>::SMEM, stream>>>(*qkv_map, p);
         break;

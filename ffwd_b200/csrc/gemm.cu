@@ -13,6 +13,7 @@
 // Two TMEM accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
 #include "gemm.cuh"
 #include "gemm_epi.cuh"
+#include "launch_util.cuh"
 #include "ptx.cuh"
 
 #include <cuda_runtime.h>
@@ -213,7 +214,7 @@ int launch_t(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap *b
              const CUtensorMap *b_lo, const GemmParams &p, int num_sms, cudaStream_t stream) {
     using C = GemmCfg<BN, PASSES>;
     auto kern = gemm_kernel<BN, PASSES, EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = set_smem_once<gemm_kernel<BN, PASSES, EPI>>(C::SMEM);
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + BM - 1) / BM) * (p.N / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;

@@ -17,6 +17,7 @@
 // No TMA load here uses cluster multicast.
 #include "gemm.cuh"
 #include "gemm_epi.cuh"
+#include "launch_util.cuh"
 #include "ptx.cuh"
 
 #include <cuda_runtime.h>
@@ -256,7 +257,7 @@ template <int EPI>
 int launch2(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p, int num_sms,
             cudaStream_t stream) {
     auto kern = gemm2_kernel<EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaError_t e = set_smem_once<gemm2_kernel<EPI>>(SMEM);
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / BN);
     int grid = 2 * tiles;

@@ -3,6 +3,8 @@ reference's CPU path: the golden fixtures it produced, and the CPU checker on
 further seeded batches.  Gates: f32 mode max-abs <= 1e-4
 and cosine >= 0.99999 per row; bf16 mode cosine >= 0.999 per row."""
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -179,3 +181,18 @@ def test_deep_long_sequences_rescale_path(model_root):
     seqs = [rng.integers(0, s.vocab, size=L).astype(np.int32) for L in lens]
     ref = of.OracleModel(d).encode_batch(seqs)
     check(model(d, "bf16").encode_batch(seqs), ref, False)
+
+
+def test_multi_device_sharding_matches_single(model_root):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    s = small_spec("qwen3-2l")
+    d = synth.ensure_model(s, model_root)
+    seqs = small_batch("qwen3-2l", n=9, max_len=400, seed=13)
+    single = native.B200Model(d, gemm_mode="bf16", devices=[0]).encode_batch(seqs)
+    n = torch.cuda.device_count()
+    multi = native.B200Model(d, gemm_mode="bf16", devices=list(range(n))).encode_batch(seqs)
+    native.lib().ffwd_b200_set_devices((ctypes.c_int * 1)(0), 1)
+    # Every sequence is computed identically on whichever device gets it.
+    assert np.array_equal(single, multi)
