@@ -89,9 +89,9 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D bf16 row-major matrix [rows, cols]; box = box_rows x box_cols.
-int make_map(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
-             uint32_t box_cols, CUtensorMapSwizzle sw) {
+// 2-D row-major matrix [rows, cols] of `esz`-byte elements; box = box_rows x box_cols.
+int make_map_dt(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                uint32_t box_cols, CUtensorMapSwizzle sw, CUtensorMapDataType dt, int esz) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         fail("cuTensorMapEncodeTiled unavailable");
@@ -99,18 +99,37 @@ int make_map(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, uint
     }
     if (rows == 0) rows = 1;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint64_t strides[1] = {cols * (uint64_t)esz};
     const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(m, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         fail("cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u", (int)r,
              (unsigned long long)rows, (unsigned long long)cols, box_rows, box_cols);
         return -1;
     }
     return 0;
+}
+
+// 2-D bf16 row-major matrix [rows, cols]; box = box_rows x box_cols.
+int make_map(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
+             uint32_t box_cols, CUtensorMapSwizzle sw) {
+    return make_map_dt(m, ptr, rows, cols, box_rows, box_cols, sw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                       2);
+}
+
+// Destination map of the two-SM GEMM's TMA epilogue (128 rows x 32 columns).
+int make_epi_map(CUtensorMap *m, const GemmParams &p) {
+    if (p.epi == kEpiResid)
+        return make_map_dt(m, p.resid, p.M, p.ldr, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
+    if (p.out_mode == kOutF32)
+        return make_map_dt(m, p.out, p.M, p.ldo, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
+    return make_map_dt(m, p.out, p.M, p.ldo, 128, 32, CU_TENSOR_MAP_SWIZZLE_64B,
+                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
 }
 
 // ------------------------------------------------------------------ model state
@@ -595,8 +614,10 @@ int gemm(Device &D, int prec, const CUtensorMap *a, const CUtensorMap *a_lo, con
     p.N = w.rows;
     p.K = w.cols;
     const int passes = prec == 0 ? 1 : prec;
-    if (passes == 1 && w.bn == 256 && use_gemm2()) {
-        LAUNCH(gemm2_launch(a, &w.map_half, p, D.num_sms, D.stream));
+    if (passes == 1 && w.bn == 256 && p.out_mode != kOutSplit && use_gemm2()) {
+        CUtensorMap mo;
+        if (make_epi_map(&mo, p)) return -1;
+        LAUNCH(gemm2_launch(a, &w.map_half, &mo, p, D.num_sms, D.stream));
         return 0;
     }
     LAUNCH(gemm_launch(a, passes >= 2 ? a_lo : nullptr, &w.map_hi, passes == 3 ? &w.map_lo : nullptr,
@@ -1281,9 +1302,10 @@ FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const voi
     p.out = y;
     p.ldo = N;
     if (passes == 1 && bn == 256 && use_gemm2()) {
-        CUtensorMap mh;
-        if (make_map(&mh, w, N, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
-        LAUNCH(gemm2_launch(&ma, &mh, p, sms, 0));
+        CUtensorMap mh, mo;
+        if (make_map(&mh, w, N, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) || make_epi_map(&mo, p))
+            return -1;
+        LAUNCH(gemm2_launch(&ma, &mh, &mo, p, sms, 0));
     } else {
         LAUNCH(gemm_launch(&ma, x_lo ? &mal : nullptr, &mb, w_lo ? &mbl : nullptr, bn, passes, p,
                            sms, 0));

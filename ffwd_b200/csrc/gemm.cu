@@ -194,7 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int mb = tile / n_blocks, nb = tile % n_blocks;
             const int grow = mb * BM + row;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
-            epilogue_tile<BN, EPI>(p, tbase, grow, grow < p.M, nb, g);
+            epi::DirectSink sink{p, grow};
+            epilogue_tile<BN, EPI>(p, tbase, grow, grow < p.M, nb, g, sink);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty_bar[a]);

@@ -63,7 +63,10 @@ int gemm_launch(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap
 // Two-SM variant (cluster of two CTAs, tcgen05.mma.cta_group::2, M = 256 per
 // pair) for single-pass bf16 with N a multiple of 256.  `b_half` maps W with a
 // box of 128 rows x 64 columns (each CTA loads its half of a 256-row tile).
-int gemm2_launch(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p, int num_sms,
-                 cudaStream_t stream);
+// `out` maps the epilogue's destination with a box of 128 rows x 32 columns:
+// the output (bf16, 64-byte swizzle; or f32, 128-byte swizzle) or, for
+// kEpiResid, the f32 residual (128-byte swizzle), which TMA adds into.
+int gemm2_launch(const CUtensorMap *a, const CUtensorMap *b_half, const CUtensorMap *out,
+                 const GemmParams &p, int num_sms, cudaStream_t stream);
 
 }  // namespace fb

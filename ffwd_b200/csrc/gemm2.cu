@@ -34,8 +34,10 @@ constexpr int kThreads = 64 + 128 * kEpiGroups;
 constexpr int A_BYTES = BM * BK * 2;         // this CTA's X rows
 constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int STAGES = 6;
-constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+constexpr int STAGES = 5;
+constexpr int OFF_STAGING = STAGES * STAGE_BYTES;
+constexpr int STAGING_BYTES = 16384;  // one 128-row x 128-byte chunk
+constexpr int SMEM = OFF_STAGING + kEpiGroups * 2 * STAGING_BYTES + 1024;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // clears the CTA-rank bit: leader's copy
 
@@ -89,10 +91,81 @@ __device__ __forceinline__ void arrive_leader(uint64_t *bar) {
                  : "memory");
 }
 
+// Epilogue output through shared memory and TMA: each 32-column row segment of
+// the warpgroup's 128 rows is written to a swizzled staging chunk (bf16: 64-byte
+// rows, 64-byte swizzle; f32: 128-byte rows, 128-byte swizzle) and stored, or
+// for the residual added (cp.reduce ... add), by one elected thread.  Two
+// chunks per warpgroup alternate; rows past M are clipped by the tensor map.
+struct TmaSink {
+    static constexpr bool kAllRows = true;  // every row takes part in the barriers
+    const GemmParams &p;
+    const CUtensorMap *map;
+    uint8_t *stage;  // this warpgroup's two chunks
+    int r, y0, g;
+    bool elected;
+    int k = 0;
+
+    __device__ __forceinline__ uint8_t *acquire() {
+        uint8_t *buf = stage + (k & 1) * STAGING_BYTES;
+        if (elected) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        named_bar(1 + g, 128);
+        return buf;
+    }
+    __device__ __forceinline__ void publish(uint8_t *buf, int col, bool reduce) {
+        fence_proxy_async_smem();
+        named_bar(1 + g, 128);
+        if (elected) {
+            if (reduce)
+                asm volatile(
+                    "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group"
+                    " [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                    "r"(smem_u32(buf)), "r"(col), "r"(y0)
+                    : "memory");
+            else
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group"
+                    " [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                    "r"(smem_u32(buf)), "r"(col), "r"(y0)
+                    : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        ++k;
+    }
+    __device__ __forceinline__ void put_f32(uint8_t *buf, const float (&v)[32]) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4 *>(buf + r * 128 + ((c ^ (r & 7)) * 16)) =
+                make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    }
+    __device__ __forceinline__ void put(const float (&v)[32], int col) {
+        uint8_t *buf = acquire();
+        if (p.out_mode == kOutF32) {
+            put_f32(buf, v);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4 *>(buf + r * 64 + ((c ^ ((r >> 1) & 3)) * 16)) =
+                    make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]),
+                               pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                               pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
+                               pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+        }
+        publish(buf, col, false);
+    }
+    __device__ __forceinline__ void add(const float (&v)[32], int col) {
+        uint8_t *buf = acquire();
+        put_f32(buf, v);
+        publish(buf, col, true);
+    }
+    __device__ __forceinline__ void finish() {
+        if (elected) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+};
+
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const GemmParams p) {
+                 const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[STAGES];
     __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -132,6 +205,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmOut);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -226,6 +300,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         const int g = (warp - 2) >> 2;
         const int row = q * 32 + lane;
+        TmaSink sink{p, &tmOut, smem + OFF_STAGING + g * 2 * STAGING_BYTES, row, 0, g,
+                     ((warp - 2) & 3) == 0 && lane == 0};
         int lt = 0;
         for (int tile = pair; tile < num_tiles; tile += n_pairs, ++lt) {
             const int a = lt & 1;
@@ -235,11 +311,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int mb = tile / n_blocks, nb = tile % n_blocks;
             const int grow = mb * 2 * BM + rank * BM + row;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
-            epilogue_tile<BN, EPI>(p, tbase, grow, grow < p.M, nb, g);
+            sink.y0 = mb * 2 * BM + rank * BM;
+            epilogue_tile<BN, EPI>(p, tbase, grow, grow < p.M, nb, g, sink);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) arrive_leader(&tempty_bar[a]);
         }
+        sink.finish();
     }
 
     tc_fence_before();
@@ -254,8 +332,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 template <int EPI>
-int launch2(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p, int num_sms,
-            cudaStream_t stream) {
+int launch2(const CUtensorMap *a, const CUtensorMap *b_half, const CUtensorMap *out,
+            const GemmParams &p, int num_sms, cudaStream_t stream) {
     auto kern = gemm2_kernel<EPI>;
     cudaError_t e = set_smem_once<gemm2_kernel<EPI>>(SMEM);
     if (e != cudaSuccess) return e;
@@ -263,23 +341,24 @@ int launch2(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p
     int grid = 2 * tiles;
     const int cap = num_sms & ~1;
     if (grid > cap) grid = cap;
-    kern<<<grid, kThreads, SMEM, stream>>>(*a, *b_half, p);
+    kern<<<grid, kThreads, SMEM, stream>>>(*a, *b_half, *out, p);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-int gemm2_launch(const CUtensorMap *a, const CUtensorMap *b_half, const GemmParams &p, int num_sms,
-                 cudaStream_t stream) {
+int gemm2_launch(const CUtensorMap *a, const CUtensorMap *b_half, const CUtensorMap *out,
+                 const GemmParams &p, int num_sms, cudaStream_t stream) {
+    if (p.out_mode == kOutSplit) return cudaErrorInvalidValue;
     if (p.M <= 0 || p.K % BK != 0 || p.N % BN != 0) return cudaErrorInvalidValue;
     if (p.epi == kEpiQKRope && (p.head_dim % 64 != 0 || BN % p.head_dim != 0))
         return cudaErrorInvalidValue;
     switch (p.epi) {
-    case kEpiStore: return launch2<kEpiStore>(a, b_half, p, num_sms, stream);
-    case kEpiGelu: return launch2<kEpiGelu>(a, b_half, p, num_sms, stream);
-    case kEpiResid: return launch2<kEpiResid>(a, b_half, p, num_sms, stream);
-    case kEpiSwiGLU: return launch2<kEpiSwiGLU>(a, b_half, p, num_sms, stream);
-    case kEpiQKRope: return launch2<kEpiQKRope>(a, b_half, p, num_sms, stream);
+    case kEpiStore: return launch2<kEpiStore>(a, b_half, out, p, num_sms, stream);
+    case kEpiGelu: return launch2<kEpiGelu>(a, b_half, out, p, num_sms, stream);
+    case kEpiResid: return launch2<kEpiResid>(a, b_half, out, p, num_sms, stream);
+    case kEpiSwiGLU: return launch2<kEpiSwiGLU>(a, b_half, out, p, num_sms, stream);
+    case kEpiQKRope: return launch2<kEpiQKRope>(a, b_half, out, p, num_sms, stream);
     }
     return cudaErrorInvalidValue;
 }

@@ -66,9 +66,29 @@ __device__ __forceinline__ void store_row32(const GemmParams &p, int row, int co
     }
 }
 
-template <int BN, int EPI>
+// Writes each thread's row segments straight to global memory.
+struct DirectSink {
+    static constexpr bool kAllRows = false;  // rows past M skip their work
+    const GemmParams &p;
+    int grow;
+    __device__ __forceinline__ void put(const float (&v)[32], int col) { store_row32(p, grow, col, v); }
+    __device__ __forceinline__ void add(const float (&v)[32], int col) {
+        float4 *r = reinterpret_cast<float4 *>(p.resid + (size_t)grow * p.ldr + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float4 x = r[i];
+            x.x += v[4 * i];
+            x.y += v[4 * i + 1];
+            x.z += v[4 * i + 2];
+            x.w += v[4 * i + 3];
+            r[i] = x;
+        }
+    }
+};
+
+template <int BN, int EPI, typename Sink>
 __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbase, int grow,
-                                              bool valid, int nb, int g) {
+                                              bool valid, int nb, int g, Sink &sink) {
     // Warpgroup g of kEpiGroups handles every kEpiGroups-th unit of the tile.
     const int n0 = nb * BN;
     if constexpr (EPI == kEpiStore || EPI == kEpiGelu) {
@@ -77,7 +97,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
             float v[32];
             tmem_ld32(tbase + c * 32, v);
             tmem_wait_ld();
-            if (!valid) continue;
+            if (!Sink::kAllRows && !valid) continue;
             const int col = n0 + c * 32;
             if (p.bias) add_bias32(v, p.bias, col);
             if constexpr (EPI == kEpiGelu) {
@@ -89,7 +109,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                     for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
                 }
             }
-            store_row32(p, grow, col, v);
+            sink.put(v, col);
         }
     } else if constexpr (EPI == kEpiResid) {
 #pragma unroll 1
@@ -97,19 +117,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
             float v[32];
             tmem_ld32(tbase + c * 32, v);
             tmem_wait_ld();
-            if (!valid) continue;
+            if (!Sink::kAllRows && !valid) continue;
             const int col = n0 + c * 32;
             if (p.bias) add_bias32(v, p.bias, col);
-            float4 *r = reinterpret_cast<float4 *>(p.resid + (size_t)grow * p.ldr + col);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                float4 x = r[i];
-                x.x += v[4 * i];
-                x.y += v[4 * i + 1];
-                x.z += v[4 * i + 2];
-                x.w += v[4 * i + 3];
-                r[i] = x;
-            }
+            sink.add(v, col);
         }
     } else if constexpr (EPI == kEpiSwiGLU) {
         const int o0 = nb * (BN / 2);
@@ -119,10 +130,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
             tmem_ld32(tbase + c * 32, g);
             tmem_ld32(tbase + BN / 2 + c * 32, u);
             tmem_wait_ld();
-            if (!valid) continue;
+            if (!Sink::kAllRows && !valid) continue;
 #pragma unroll
             for (int i = 0; i < 32; ++i) g[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
-            store_row32(p, grow, o0 + c * 32, g);
+            sink.put(g, o0 + c * 32);
         }
     } else if constexpr (EPI == kEpiQKRope) {
         const int hd = p.head_dim;
@@ -141,9 +152,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                     float v[32];
                     tmem_ld32(tbase + h0 + c * 32, v);
                     tmem_wait_ld();
-                    if (!valid) continue;
+                    if (!Sink::kAllRows && !valid) continue;
                     if (p.bias) add_bias32(v, p.bias, col0 + c * 32);
-                    store_row32(p, grow, col0 + c * 32, v);
+                    sink.put(v, col0 + c * 32);
                 }
                 continue;
             }
@@ -170,7 +181,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                 tmem_ld32(tbase + h0 + c * 32, x1);
                 tmem_ld32(tbase + h0 + half + c * 32, x2);
                 tmem_wait_ld();
-                if (!valid) continue;
+                if (!Sink::kAllRows && !valid) continue;
                 if (p.bias) {
                     add_bias32(x1, p.bias, col0 + c * 32);
                     add_bias32(x2, p.bias, col0 + half + c * 32);
@@ -201,8 +212,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                         x2[4 * i + u] = b * cc[u] + a * ss[u];
                     }
                 }
-                store_row32(p, grow, col0 + c * 32, x1);
-                store_row32(p, grow, col0 + half + c * 32, x2);
+                sink.put(x1, col0 + c * 32);
+                sink.put(x2, col0 + half + c * 32);
             }
         }
     }
