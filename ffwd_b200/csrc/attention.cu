@@ -1,19 +1,24 @@
 // Varlen attention kernels (see attention.cuh).
 //
 // Tensor-core kernel, one CTA per work item = up to two query blocks (128
-// query rows of one head each) that share one key/value head; 384 threads:
-//   warp 0      TMA producer: both Q tiles once, then K_0 V_0 K_1 V_1 ... into a
-//               three-slot shared-memory ring.
-//   warp 1      allocates TMEM (S0 | S1 | O0 | O1) and one lane issues the
-//               tcgen05.mma: S_w = Q_w K_j^T (M=128, N=128) and O_w += P_w V_j
-//               (M=128, N=head_dim, V read as an MN-major operand from its TMA
-//               tile), interleaving the two blocks so the tensor cores work on
-//               one block while the other block's softmax runs.
-//   warps 4-7   softmax for block 0, warps 8-11 for block 1: one thread per
-//               query row reads its score row from TMEM, masks (length, causal),
-//               writes P_w = exp2(s - m) as bf16 into a 128-byte-swizzled shared
-//               tile and keeps the row sum.  O stays in TMEM; it is rescaled in
-//               place only when the running row max grows by more than 2^8.
+// query rows of one head each) that share one key/value head; keys in tiles of
+// 64.  384 threads:
+//   warps 0-3   softmax of block 0, warps 4-7 softmax of block 1: one thread per
+//               query row; reads its 64 scores of a key tile from TMEM, masks
+//               (length, causal), writes P = exp2(s - m) as packed bf16 back into
+//               the first 32 columns of its S buffer in TMEM and keeps the row
+//               sum.  O accumulates in TMEM and is rescaled in place only when the
+//               running row max grows by more than 2^8 (decided per warp:
+//               tcgen05.ld/st are collective).
+//   warp 8      TMA producer: both Q tiles once, then K_0 V_0 K_1 V_1 ... into a
+//               six-slot ring of 64-key tiles.
+//   warp 9      allocates TMEM (O0 | O1 | S0a S0b S1a S1b) and one lane issues
+//               tcgen05.mma.  S is double-buffered per block: S_w(j+2) is computed
+//               while the softmax works on S_w(j); O += P V takes P straight from
+//               TMEM (tcgen05.mma with A in TMEM), so only K and V are read from
+//               shared memory.  P_w(j) aliases S buffer j % 2: the MMA issuer
+//               issues PV_w(j) before S_w(j + 2) (one thread's MMAs run in issue
+//               order), and the softmax writes P only after S_w(j) was read.
 // Masking follows the packed layout: key k of sequence b is visible to query q
 // iff k < len(b) and (bidirectional or k <= q).
 #include "attention.cuh"
@@ -25,15 +30,12 @@
 namespace fb {
 namespace {
 
-constexpr int kTile = 128;  // query rows and keys per tile
-// Warpgroup 0 (warps 0-3): softmax of block 0; warpgroup 1 (warps 4-7): softmax
-// of block 1; warp 8: producer; warp 9: MMA issuer (warps 10-11 only pad the CTA
-// to three warpgroups).  384 threads leave 168 registers per thread, enough for
-// a softmax thread to hold its whole 128-score row.
+constexpr int kTile = 128;  // query rows per block (and per AttnItem tile)
+constexpr int kKT = 64;     // keys per key tile
 constexpr int kAttnThreads = 384;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kRingSlots = 3;
+constexpr int kRingSlots = 10;
 constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
 
 template <int D>
@@ -43,54 +45,40 @@ struct AttnCfg {
     static constexpr int ROWB = BOXC * 2;                            // bytes per smem row
     static constexpr uint32_t LAYOUT = D == 32 ? kLayoutSW64 : kLayoutSW128;
     static constexpr int SBO = 8 * ROWB;                             // 8-row atom
-    static constexpr int BOX_BYTES = kTile * ROWB;
-    static constexpr int TILE_BYTES = NBOX * BOX_BYTES;              // Q, K or V tile
-    static constexpr int P_BYTES = kTile * kTile * 2;                // 2 SW128 blocks
+    static constexpr int QBOX = kTile * ROWB;                        // Q box (128 rows)
+    static constexpr int Q_BYTES = NBOX * QBOX;
+    static constexpr int KVBOX = kKT * ROWB;                         // K/V box (64 rows)
+    static constexpr int KV_BYTES = NBOX * KVBOX;
     static constexpr int OFF_Q = 0;                                  // Q0, Q1
-    static constexpr int OFF_RING = 2 * TILE_BYTES;
-    static constexpr int OFF_P = OFF_RING + kRingSlots * TILE_BYTES; // P0, P1
-    static constexpr int OFF_MISC = OFF_P + 2 * P_BYTES;             // barriers + row exchange
-    static constexpr int MISC_BYTES = 256 + 2 * 2 * kTile * 4;
-    static constexpr int USED = OFF_MISC + MISC_BYTES;
-    // Slack for aligning the dynamic window to 1024 bytes where it fits the
-    // 227 KB limit; for head_dim 128 the window must already be aligned
-    // (checked at run time).
-    static constexpr int PAD = USED + 1024 <= 232448 - 1024 ? 1024 : 0;
-    static constexpr int SMEM = USED + PAD;
-    static constexpr int TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D, ..)
+    static constexpr int OFF_RING = 2 * Q_BYTES;
+    static constexpr int SMEM = OFF_RING + kRingSlots * KV_BYTES + 1024;
+    static constexpr int TMEM_COLS = 512;  // O0 [0,D) O1 [D,2D) S[w][b] at 256 + (2w + b) 64
 };
 
-// K-major operand (Q or K tile): k-step `kk` covers elements [16 kk, 16 kk + 16).
+// K-major operand (Q or K tile) descriptor of k-step 0; k-step kk adds koff(kk).
 template <int D>
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base) {
     using C = AttnCfg<D>;
-    const int e = kk * 16;
-    const uint32_t addr = base + (e / C::BOXC) * C::BOX_BYTES + (e % C::BOXC) * 2;
-    return smem_desc(addr, 16, C::SBO, C::LAYOUT);
+    return smem_desc(base, 16, C::SBO, C::LAYOUT);
 }
 
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
+                   const AttnParams p) {
     using C = AttnCfg<D>;
     extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t q_full;
+    __shared__ __align__(8) uint64_t ring_full[kRingSlots], ring_empty[kRingSlots];
+    __shared__ __align__(8) uint64_t s_full[2][2], s_free[2][2], p_full[2][2], pv_done[2][2];
+    __shared__ __align__(8) uint64_t drain;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    if (smem - smem_raw > C::PAD) {  // window not aligned and no slack: refuse
-        if (threadIdx.x == 0) set_error(p.err, kErrSmemAlign);
-        return;
-    }
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_MISC);
-    uint64_t &q_full = bars[0];
-    uint64_t *ring_full = bars + 1, *ring_empty = bars + 1 + kRingSlots;
-    uint64_t *s_full = bars + 1 + 2 * kRingSlots, *p_full = s_full + 2, *o_final = s_full + 4;
-    uint64_t &drain = s_full[6];
-    uint32_t &tmem_base_sh = *reinterpret_cast<uint32_t *>(smem + C::OFF_MISC + 192);
-    int &abort_sh = *reinterpret_cast<int *>(smem + C::OFF_MISC + 196);
-    // Row exchange between the two halves of a block: [block][half][row].
-    float(*red)[2][kTile] = reinterpret_cast<float(*)[2][kTile]>(smem + C::OFF_MISC + 256);
 
     const AttnItem item = p.items[blockIdx.x];
     const bool two = item.qt1 >= 0;
@@ -99,7 +87,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int L = p.offsets[item.seq + 1] - seq0;
     const int qt_max = two ? max(item.qt0, item.qt1) : item.qt0;
     const int kend = p.causal ? min(qt_max * kTile + kTile, L) : L;
-    const int n_kt = (kend + kTile - 1) / kTile;
+    const int n_kt = (kend + kKT - 1) / kKT;
 
     if (threadIdx.x == 0) {
         mbar_init(&q_full, 1);
@@ -107,17 +95,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(&ring_full[i], 1);
             mbar_init(&ring_empty[i], 1);
         }
-        for (int w = 0; w < 2; ++w) {
-            mbar_init(&s_full[w], 1);
-            mbar_init(&p_full[w], 4);
-            mbar_init(&o_final[w], 1);
-        }
+        for (int w = 0; w < 2; ++w)
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&s_full[w][b], 1);
+                mbar_init(&s_free[w][b], 4);
+                mbar_init(&p_full[w][b], 4);
+                mbar_init(&pv_done[w][b], 1);
+            }
         mbar_init(&drain, 1);
         abort_sh = 0;
-        tmem_base_sh = 0;
         fence_barrier_init();
     }
-    if (warp == kProducerWarp && lane == 0) tma_prefetch_desc(&tm);
+    if (warp == kProducerWarp && lane == 0) {
+        tma_prefetch_desc(&tmq);
+        tma_prefetch_desc(&tmkv);
+    }
     if (warp == kMmaWarp) {
         tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
         tmem_relinquish();
@@ -129,20 +121,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
     uint8_t *sQ = smem + C::OFF_Q;
     uint8_t *sRing = smem + C::OFF_RING;
-    uint8_t *sP = smem + C::OFF_P;
 
     if (warp == kProducerWarp) {
         if (lane == 0) {
             // ------------------------------------------------------------ producer
             int issued = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(&q_full, (two ? 2 : 1) * C::TILE_BYTES);
+            mbar_arrive_expect_tx(&q_full, (two ? 2 : 1) * C::Q_BYTES);
             for (int b = 0; b < C::NBOX; ++b)
-                tma_load_2d(sQ + b * C::BOX_BYTES, &tm, &q_full,
-                            p.q_col0 + item.h0 * D + b * C::BOXC, seq0 + item.qt0 * kTile);
+                tma_load_2d(sQ + b * C::QBOX, &tmq, &q_full, p.q_col0 + item.h0 * D + b * C::BOXC,
+                            seq0 + item.qt0 * kTile);
             if (two)
                 for (int b = 0; b < C::NBOX; ++b)
-                    tma_load_2d(sQ + C::TILE_BYTES + b * C::BOX_BYTES, &tm, &q_full,
+                    tma_load_2d(sQ + C::Q_BYTES + b * C::QBOX, &tmq, &q_full,
                                 p.q_col0 + item.h1 * D + b * C::BOXC, seq0 + item.qt1 * kTile);
             for (int i = 0; i < 2 * n_kt; ++i) {
                 const int slot = i % kRingSlots;
@@ -152,11 +143,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     break;
                 }
                 const int col = ((i & 1) ? p.v_col0 : p.k_col0) + kvh * D;
-                const int row = seq0 + (i >> 1) * kTile;
-                mbar_arrive_expect_tx(&ring_full[slot], C::TILE_BYTES);
+                const int row = seq0 + (i >> 1) * kKT;
+                mbar_arrive_expect_tx(&ring_full[slot], C::KV_BYTES);
                 for (int b = 0; b < C::NBOX; ++b)
-                    tma_load_2d(sRing + slot * C::TILE_BYTES + b * C::BOX_BYTES, &tm,
-                                &ring_full[slot], col + b * C::BOXC, row);
+                    tma_load_2d(sRing + slot * C::KV_BYTES + b * C::KVBOX, &tmkv, &ring_full[slot],
+                                col + b * C::BOXC, row);
                 ++issued;
             }
             if (!ok) {
@@ -169,80 +160,88 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
-            constexpr uint32_t IDESC_S = idesc_f16(128, 128, 1, 1, 0, 0);
+            constexpr uint32_t IDESC_S = idesc_f16(128, kKT, 1, 1, 0, 0);
             constexpr uint32_t IDESC_O = idesc_f16(128, D, 1, 1, 0, 1);
-            const uint32_t aQ = smem_u32(sQ);
-            const uint32_t aRing = smem_u32(sRing);
-            const uint32_t aP = smem_u32(sP);
             const int nw = two ? 2 : 1;
-            auto slot_of = [](int i) { return i % kRingSlots; };
+            // Descriptors are linear in the start address (16-byte units in the
+            // low bits): each operand's descriptor is built once and offset.
+            const uint64_t dQ = kmajor_desc<D>(smem_u32(sQ));
+            const uint64_t dRingK = kmajor_desc<D>(smem_u32(sRing));
+            const uint64_t dRingV = smem_desc(smem_u32(sRing), C::KVBOX, C::SBO, C::LAYOUT);
+            auto kk_off = [](int kk) -> uint64_t {  // K-major k-step offset (16-byte units)
+                const int e = kk * 16;
+                return (uint64_t)(((e / C::BOXC) * C::QBOX + (e % C::BOXC) * 2) >> 4);
+            };
+            auto kk_offk = [](int kk) -> uint64_t {
+                const int e = kk * 16;
+                return (uint64_t)(((e / C::BOXC) * C::KVBOX + (e % C::BOXC) * 2) >> 4);
+            };
             auto wait_slot = [&](int i) -> bool {
                 return mbar_wait(&ring_full[i % kRingSlots], (i / kRingSlots) & 1, p.err, &abort_sh);
             };
-            // Descriptors are linear in the start address (16-byte units in the low
-            // bits), so each operand's descriptor is built once and offset per MMA.
-            const uint64_t dQ = kmajor_desc<D>(aQ, 0);
-            const uint64_t dRingK = kmajor_desc<D>(aRing, 0);
-            const uint64_t dRingV = smem_desc(aRing, C::BOX_BYTES, C::SBO, C::LAYOUT);
-            const uint64_t dP = smem_desc(aP, 16, 1024, kLayoutSW128);
-            auto koff = [](int kk) -> uint64_t {  // K-major k-step offset (16-byte units)
-                const int e = kk * 16;
-                return (uint64_t)(((e / C::BOXC) * C::BOX_BYTES + (e % C::BOXC) * 2) >> 4);
-            };
             auto issue_s = [&](int w, int j) {
-                const uint64_t dK = dRingK + (uint64_t)((slot_of(2 * j) * C::TILE_BYTES) >> 4);
-                const uint64_t dQw = dQ + (uint64_t)((w * C::TILE_BYTES) >> 4);
-                const uint32_t d = tmem_base + w * 128;
+                const uint64_t dK = dRingK + (uint64_t)((((2 * j) % kRingSlots) * C::KV_BYTES) >> 4);
+                const uint64_t dQw = dQ + (uint64_t)((w * C::Q_BYTES) >> 4);
+                const uint32_t d = tmem_base + 256 + (2 * w + (j & 1)) * kKT;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(d, dQw + koff(kk), dK + koff(kk), IDESC_S, kk != 0);
+                    umma_f16(d, dQw + kk_off(kk), dK + kk_offk(kk), IDESC_S, kk != 0);
             };
             auto issue_pv = [&](int w, int j) {
-                const uint64_t dV = dRingV + (uint64_t)((slot_of(2 * j + 1) * C::TILE_BYTES) >> 4);
-                const uint64_t dPw = dP + (uint64_t)((w * C::P_BYTES) >> 4);
-                const uint32_t d = tmem_base + 256 + w * D;
+                const uint64_t dV =
+                    dRingV + (uint64_t)((((2 * j + 1) % kRingSlots) * C::KV_BYTES) >> 4);
+                const uint32_t tP = tmem_base + 256 + (2 * w + (j & 1)) * kKT;
+                const uint32_t d = tmem_base + w * D;
 #pragma unroll
-                for (int kk = 0; kk < kTile / 16; ++kk)
-                    umma_f16(d, dPw + (uint64_t)(((kk / 4) * (kTile * 128) + (kk % 4) * 32) >> 4),
-                             dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O, (j | kk) != 0);
+                for (int kk = 0; kk < kKT / 16; ++kk)
+                    umma_f16_ts(d, tP + kk * 8, dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O,
+                                (j | kk) != 0);
             };
-            bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh) && wait_slot(0);
-            if (ok) {
+            bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh);
+            // Prologue: S(0) and S(1) for both blocks.
+            for (int j = 0; ok && j < 2 && j < n_kt; ++j) {
+                if (!wait_slot(2 * j)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 for (int w = 0; w < nw; ++w) {
-                    issue_s(w, 0);
-                    umma_commit(&s_full[w]);
+                    issue_s(w, j);
+                    umma_commit(&s_full[w][j & 1]);
                 }
-                umma_commit(&ring_empty[slot_of(0)]);
+                umma_commit(&ring_empty[(2 * j) % kRingSlots]);
             }
             for (int j = 0; ok && j < n_kt; ++j) {
-                const bool more = j + 1 < n_kt;
+                const int b = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                const bool more = j + 2 < n_kt;
                 if (!wait_slot(2 * j + 1)) {
                     ok = false;
                     break;
                 }
-                for (int w = 0; w < nw; ++w) {
-                    if (!mbar_wait(&p_full[w], j & 1, p.err, &abort_sh)) {
+                for (int w = 0; w < nw && ok; ++w) {
+                    if (!mbar_wait(&p_full[w][b], ph, p.err, &abort_sh)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     issue_pv(w, j);
+                    umma_commit(&pv_done[w][b]);
                     if (more) {
-                        if (w == 0 && !wait_slot(2 * j + 2)) {
+                        // S_w(j+2) reuses S buffer b once the softmax has read S_w(j).
+                        if (!mbar_wait(&s_free[w][b], ph, p.err, &abort_sh) ||
+                            (w == 0 && !wait_slot(2 * j + 4))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        issue_s(w, j + 1);
-                        umma_commit(&s_full[w]);
-                    } else {
-                        umma_commit(&o_final[w]);
+                        issue_s(w, j + 2);
+                        umma_commit(&s_full[w][b]);
                     }
                 }
                 if (!ok) break;
-                umma_commit(&ring_empty[slot_of(2 * j + 1)]);
-                if (more) umma_commit(&ring_empty[slot_of(2 * j + 2)]);
+                umma_commit(&ring_empty[(2 * j + 1) % kRingSlots]);
+                if (more) umma_commit(&ring_empty[(2 * j + 4) % kRingSlots]);
             }
             if (!ok) {
                 umma_commit(&drain);
@@ -252,8 +251,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
     } else if (warp < 8) {
         // ---------------------------------------------------------------- softmax
-        // One thread per query row: the row's 128 scores of a tile are read from
-        // TMEM once (four loads in flight) and kept in registers.
         const int w = warp >> 2;
         if (w == 0 || two) {
             const int quad = warp & 3;
@@ -263,29 +260,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int q = qt * kTile + r;
             const float sl2 = p.scale * 1.4426950408889634f;
             const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-            const uint32_t tS = tmem_base + lane_off + w * 128;
-            const uint32_t tO = tmem_base + lane_off + 256 + w * D;
-            uint8_t *rowp0 = sP + w * C::P_BYTES + r * 128;
+            const uint32_t tO = tmem_base + lane_off + w * D;
             float m_used = -INFINITY, l = 0.0f;
             bool ok = true;
             for (int j = 0; j < n_kt; ++j) {
-                if (!mbar_wait(&s_full[w], j & 1, p.err, &abort_sh)) {
+                const int b = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&s_full[w][b], ph, p.err, &abort_sh)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                float v0[32], v1[32], v2[32], v3[32];
+                const uint32_t tS = tmem_base + lane_off + 256 + (2 * w + b) * kKT;
+                float v0[32], v1[32];
                 tmem_ld32(tS, v0);
                 tmem_ld32(tS + 32, v1);
-                tmem_ld32(tS + 64, v2);
-                tmem_ld32(tS + 96, v3);
                 tmem_wait_ld();
-#define V(i) ((i) < 32 ? v0[(i)] : (i) < 64 ? v1[(i) - 32] : (i) < 96 ? v2[(i) - 64] : v3[(i) - 96])
-                const int k0 = j * kTile;
+#define V(i) ((i) < 32 ? v0[(i)] : v1[(i) - 32])
+                const int k0 = j * kKT;
                 // Tiles wholly inside the sequence and below the diagonal need no mask.
-                if (k0 + kTile > L || (p.causal && k0 + kTile - 1 > qt * kTile)) {
+                if (k0 + kKT > L || (p.causal && k0 + kKT - 1 > qt * kTile)) {
 #pragma unroll
-                    for (int i = 0; i < 128; ++i) {
+                    for (int i = 0; i < kKT; ++i) {
                         const int key = k0 + i;
                         if (!(key < L && (!p.causal || key <= q))) V(i) = -INFINITY;
                     }
@@ -294,17 +290,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 8; ++i) mxa[i] = V(i);
 #pragma unroll
-                for (int i = 8; i < 128; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], V(i));
+                for (int i = 8; i < kKT; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], V(i));
                 const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
                                        fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
                 const float m_new = fmaxf(m_used, mx * sl2);
-                // tcgen05.ld/st are warp-collective: the rescale decision is taken per
-                // warp (any row over the threshold), each row by its own factor.
                 if (j == 0) {
                     m_used = m_new;
                 } else if (__any_sync(0xffffffffu, m_new > m_used + kRescaleLog2)) {
-                    // O_w is stable here: PV_{j-1} completed before S_j was published,
-                    // and PV_j waits for this block's P_j.
+                    // O_w may only change once PV_w(j-1) has completed; PV_w(j)
+                    // waits for this block's P_w(j).
+                    if (!mbar_wait(&pv_done[w][(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, &abort_sh)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
                     const float alpha = ex2_approx(m_used - m_new);
 #pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
@@ -319,32 +318,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     l *= alpha;
                     m_used = m_new;
                 }
+                // P_w(j) overwrites the S_w(j) columns just read (P_w(j-2) in the
+                // other buffer may still be in use by PV_w(j-2)).
+                uint32_t pk[32];
                 float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int ch = 0; ch < 16; ++ch) {  // 16-byte chunk = 8 keys
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float p0 = ex2_approx(fmaf(V(8 * ch + 2 * u), sl2, -m_used));
-                        const float p1 = ex2_approx(fmaf(V(8 * ch + 2 * u + 1), sl2, -m_used));
-                        la[u] += p0 + p1;
-                        pk[u] = pack_bf16x2(p0, p1);
-                    }
-                    // Keys [8 ch, 8 ch + 8) -> block ch / 8, swizzled chunk ch % 8.
-                    *reinterpret_cast<uint4 *>(rowp0 + (ch >> 3) * (kTile * 128) +
-                                               (((ch & 7) ^ (r & 7)) * 16)) =
-                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    // Bound the live range: exp / pack / store 32 keys at a time.
-                    if ((ch & 3) == 3) asm volatile("" ::: "memory");
+                for (int i = 0; i < 32; ++i) {
+                    const float p0 = ex2_approx(fmaf(V(2 * i), sl2, -m_used));
+                    const float p1 = ex2_approx(fmaf(V(2 * i + 1), sl2, -m_used));
+                    la[i & 3] += p0 + p1;
+                    pk[i] = pack_bf16x2(p0, p1);
                 }
 #undef V
+                tmem_st32u(tS, pk);
+                tmem_wait_st();
                 l += (la[0] + la[1]) + (la[2] + la[3]);
                 tc_fence_before();
-                fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&p_full[w]);
+                if (lane == 0) {
+                    mbar_arrive(&s_free[w][b]);
+                    mbar_arrive(&p_full[w][b]);
+                }
             }
-            if (ok && mbar_wait(&o_final[w], 0, p.err, &abort_sh)) {
+            const int jl = n_kt - 1;
+            if (ok && mbar_wait(&pv_done[w][jl & 1], (jl >> 1) & 1, p.err, &abort_sh)) {
                 tc_fence_after();
                 const float inv = l > 0.0f ? 1.0f / l : 0.0f;
                 __nv_bfloat16 *orow = p.out + (size_t)(seq0 + q) * p.ldo + h * D;
@@ -464,7 +461,8 @@ __global__ void __launch_bounds__(kF32Threads)
 
 }  // namespace
 
-int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStream_t stream) {
+int attention_tc_launch(const CUtensorMap *q_map, const CUtensorMap *kv_map, const AttnParams &p,
+                        cudaStream_t stream) {
     if (p.n_items <= 0) return cudaSuccess;
     dim3 grid(p.n_items);
     cudaError_t e;
@@ -472,17 +470,17 @@ int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStr
     case 32:
         e = set_smem_once<attn_tc_kernel<32>>(AttnCfg<32>::SMEM);
         if (e != cudaSuccess) return e;
-        attn_tc_kernel<32><<<grid, kAttnThreads, AttnCfg<32>::SMEM, stream>>>(*qkv_map, p);
+        attn_tc_kernel<32><<<grid, kAttnThreads, AttnCfg<32>::SMEM, stream>>>(*q_map, *kv_map, p);
         break;
     case 64:
         e = set_smem_once<attn_tc_kernel<64>>(AttnCfg<64>::SMEM);
         if (e != cudaSuccess) return e;
-        attn_tc_kernel<64><<<grid, kAttnThreads, AttnCfg<64>::SMEM, stream>>>(*qkv_map, p);
+        attn_tc_kernel<64><<<grid, kAttnThreads, AttnCfg<64>::SMEM, stream>>>(*q_map, *kv_map, p);
         break;
     case 128:
         e = set_smem_once<attn_tc_kernel<128>>(AttnCfg<128>::SMEM);
         if (e != cudaSuccess) return e;
-        attn_tc_kernel<128><<<grid, kAttnThreads, AttnCfg<128>::SMEM, stream>>>(*qkv_map, p);
+        attn_tc_kernel<128><<<grid, kAttnThreads, AttnCfg<128>::SMEM, stream>>>(*q_map, *kv_map, p);
         break;
     default:
         return cudaErrorInvalidValue;

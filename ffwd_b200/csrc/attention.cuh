@@ -56,10 +56,11 @@ int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int 
 int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, const int *h_offsets,
                           int batch);
 
-// Tensor-core path.  `qkv_map`: 2-D bf16 map over the qkv matrix with a box of
-// 128 rows x min(head_dim, 64) columns (128-byte swizzle, or 64-byte for
-// head_dim 32).
-int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStream_t stream);
+// Tensor-core path.  `q_map` / `kv_map`: 2-D bf16 maps over the qkv matrix
+// with boxes of 128 / 64 rows x min(head_dim, 64) columns (128-byte swizzle, or
+// 64-byte for head_dim 32).
+int attention_tc_launch(const CUtensorMap *q_map, const CUtensorMap *kv_map, const AttnParams &p,
+                        cudaStream_t stream);
 
 // f32 CUDA-core path for the exact (f32 / split-bf16) precision mode.  Items
 // here use query tiles of attention_f32_qtile(head_dim) rows.

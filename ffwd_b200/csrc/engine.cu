@@ -171,7 +171,7 @@ struct Workspace {
 // re-issued for timing).
 struct FwdState {
     int T = 0, B = 0, n_items = 0;
-    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv;
+    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv, m_kv;
     AttnParams ap{};
 };
 
@@ -667,8 +667,10 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
                   make_map(&fs.m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
                   make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
         return -1;
-    if (!split && make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
-                           c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!split && (make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
+                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ||
+                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, std::min(c.head_dim, 64),
+                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
         return -1;
 
     AttnParams &ap = fs.ap;
@@ -746,7 +748,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
         if (split)
             LAUNCH(attention_f32_launch(fs.ap, s));
         else
-            LAUNCH(attention_tc_launch(&fs.m_qkv, fs.ap, s));
+            LAUNCH(attention_tc_launch(&fs.m_qkv, &fs.m_kv, fs.ap, s));
         return 0;
     case kOpO: {  // output projection + residual (+ bias)
         GemmParams p{};
@@ -1471,8 +1473,10 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
                   make_map(&fs.m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
                   make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
         return -1;
-    if (!split && make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
-                           c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!split && (make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
+                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ||
+                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, std::min(c.head_dim, 64),
+                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
         return -1;
     AttnParams &ap = fs.ap;
     ap.offsets = w.offsets;
