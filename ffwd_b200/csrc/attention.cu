@@ -1,24 +1,29 @@
 // Varlen attention kernels (see attention.cuh).
 //
-// Tensor-core kernel, one CTA per work item = up to two query blocks (128
-// query rows of one head each) that share one key/value head; keys in tiles of
-// 64.  384 threads:
-//   warps 0-3   softmax of block 0, warps 4-7 softmax of block 1: one thread per
-//               query row; reads its 64 scores of a key tile from TMEM, masks
-//               (length, causal), writes P = exp2(s - m) as packed bf16 back into
-//               the first 32 columns of its S buffer in TMEM and keeps the row
-//               sum.  O accumulates in TMEM and is rescaled in place only when the
-//               running row max grows by more than 2^8 (decided per warp:
-//               tcgen05.ld/st are collective).
-//   warp 8      TMA producer: both Q tiles once, then K_0 V_0 K_1 V_1 ... into a
-//               six-slot ring of 64-key tiles.
-//   warp 9      allocates TMEM (O0 | O1 | S0a S0b S1a S1b) and one lane issues
-//               tcgen05.mma.  S is double-buffered per block: S_w(j+2) is computed
-//               while the softmax works on S_w(j); O += P V takes P straight from
-//               TMEM (tcgen05.mma with A in TMEM), so only K and V are read from
-//               shared memory.  P_w(j) aliases S buffer j % 2: the MMA issuer
-//               issues PV_w(j) before S_w(j + 2) (one thread's MMAs run in issue
-//               order), and the softmax writes P only after S_w(j) was read.
+// Tensor-core kernel: persistent, one CTA per SM.  A work item is a pair of
+// query blocks (128 query rows each) that read the same keys and values: the
+// two query heads of one key/value head (grouped-query models), or two
+// adjacent query tiles of one head.  Each K/V tile is loaded once and used by
+// both blocks, which halves the K/V traffic.  CTAs claim items in list order
+// from a global counter; the list keeps the items of one (sequence, key/value
+// head) together, so CTAs that run at the same time share K/V in L2.
+// 384 threads:
+//   warps 0-3   softmax of block 0, warps 4-7 block 1: one thread per query
+//               row reads its 128 scores from TMEM, masks (length, causal),
+//               writes P = exp2(s - m) as packed bf16 over the first half of
+//               the same score columns and keeps the row sum.  O accumulates in
+//               TMEM and is rescaled in place only when the running row max
+//               grows by more than 2^8 (decided per warp: tcgen05.ld/st are
+//               warp-collective).  At the end of an item it writes O / l.
+//   warp 8      producer: claims items, publishes them to the other roles,
+//               loads both Q tiles (double-buffered by item) and then
+//               K_0 V_0 K_1 V_1 ... into a shared-memory ring.
+//   warp 9      allocates TMEM (S0 | S1 | O0 | O1); one lane issues tcgen05.mma
+//               in the order PV0(j) S0(j+1) PV1(j) S1(j+1): the tensor pipe works
+//               on one block while the other block's softmax runs.  S_b(j+1)
+//               overwrites the columns PV_b(j) reads P from; one thread's MMAs
+//               execute in issue order, so that is safe.  After an item's last
+//               tile the next item's first S follows directly.
 // Masking follows the packed layout: key k of sequence b is visible to query q
 // iff k < len(b) and (bidirectional or k <= q).
 #include "attention.cuh"
@@ -26,17 +31,18 @@
 #include "ptx.cuh"
 
 #include <algorithm>
+#include <vector>
 
 namespace fb {
 namespace {
 
-constexpr int kTile = 128;  // query rows per block (and per AttnItem tile)
-constexpr int kKT = 64;     // keys per key tile
+constexpr int kTile = 128;  // query rows per block and keys per key tile
 constexpr int kAttnThreads = 384;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kRingSlots = 10;
+constexpr int kItemSlots = 4;  // published-item ring
 constexpr float kRescaleLog2 = 8.0f;  // lazy O rescale threshold (factor 256)
+constexpr int kSmemCap = 232448 - 2048;  // dynamic shared memory budget (static part reserved)
 
 template <int D>
 struct AttnCfg {
@@ -45,33 +51,75 @@ struct AttnCfg {
     static constexpr int ROWB = BOXC * 2;                            // bytes per smem row
     static constexpr uint32_t LAYOUT = D == 32 ? kLayoutSW64 : kLayoutSW128;
     static constexpr int SBO = 8 * ROWB;                             // 8-row atom
-    static constexpr int QBOX = kTile * ROWB;                        // Q box (128 rows)
-    static constexpr int Q_BYTES = NBOX * QBOX;
-    static constexpr int KVBOX = kKT * ROWB;                         // K/V box (64 rows)
-    static constexpr int KV_BYTES = NBOX * KVBOX;
-    static constexpr int OFF_Q = 0;                                  // Q0, Q1
-    static constexpr int OFF_RING = 2 * Q_BYTES;
-    static constexpr int SMEM = OFF_RING + kRingSlots * KV_BYTES + 1024;
-    static constexpr int TMEM_COLS = 512;  // O0 [0,D) O1 [D,2D) S[w][b] at 256 + (2w + b) 64
+    static constexpr int BOX_BYTES = kTile * ROWB;                   // 128-row box
+    static constexpr int TILE_BYTES = NBOX * BOX_BYTES;              // Q, K or V tile
+    static constexpr int OFF_Q = 0;  // Q[item parity][block]
+    static constexpr int OFF_RING = 4 * TILE_BYTES;
+    static constexpr int RING0 = (kSmemCap - 1024 - OFF_RING) / TILE_BYTES;
+    static constexpr int RING = RING0 > 8 ? 8 : RING0;               // K/V ring slots
+    static constexpr int SMEM = OFF_RING + RING * TILE_BYTES + 1024;
+    static constexpr int TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512)
+    static constexpr int CW = D < 32 ? D : 32;
+    static_assert(RING >= 3, "K/V ring too small");
 };
 
-// K-major operand (Q or K tile) descriptor of k-step 0; k-step kk adds koff(kk).
-template <int D>
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base) {
-    using C = AttnCfg<D>;
-    return smem_desc(base, 16, C::SBO, C::LAYOUT);
+// exp2 on the FMA pipe for a share of the softmax elements, so that the
+// MUFU unit is not the bound: x = n + f with n = round(x), f in [-1/2, 1/2];
+// 2^f by a degree-3 polynomial (coefficients fitted to 2^f on [-1/2, 1/2] by
+// iteratively reweighted least squares in relative error: max relative error
+// 7.5e-5, far below the bf16 rounding of P), 2^n added to the exponent field.
+// x is clamped at -126 (-inf -> about 1e-38, which vanishes in the row sum).
+__device__ __forceinline__ float exp2_fma(float x) {
+    x = fmaxf(x, -126.0f);
+    const float t = x + 12582912.0f;  // 1.5 * 2^23: round(x) lands in the low mantissa bits
+    const float f = x - (t - 12582912.0f);
+    const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.242611125f), f, 0.693260968f), f,
+                         0.999928057f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// Item geometry, recomputed by every role from the shared work list.
+struct ItemGeo {
+    int seq0, L, kvh, n_kt;
+    int qt[2], h[2];
+    bool store1;  // block 1 is a real block (else it repeats block 0, unstored)
+};
+
+__device__ __forceinline__ ItemGeo item_geo(const AttnParams &p, int idx) {
+    const AttnItem it = p.items[idx];
+    ItemGeo g;
+    g.seq0 = p.offsets[it.seq];
+    g.L = p.offsets[it.seq + 1] - g.seq0;
+    g.store1 = it.qt1 >= 0;
+    g.qt[0] = it.qt0;
+    g.h[0] = it.h0;
+    g.qt[1] = g.store1 ? it.qt1 : it.qt0;
+    g.h[1] = g.store1 ? it.h1 : it.h0;
+    g.kvh = it.h0 / (p.n_heads / p.n_kv_heads);
+    const int qmax = max(g.qt[0], g.qt[1]);
+    const int kend = p.causal ? min(qmax * kTile + kTile, g.L) : g.L;
+    g.n_kt = (kend + kTile - 1) / kTile;
+    return g;
 }
 
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
-                   const AttnParams p) {
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     using C = AttnCfg<D>;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t q_full;
-    __shared__ __align__(8) uint64_t ring_full[kRingSlots], ring_empty[kRingSlots];
-    __shared__ __align__(8) uint64_t s_full[2][2], s_free[2][2], p_full[2][2], pv_done[2][2];
+    __shared__ __align__(8) uint64_t item_full[kItemSlots];
+    __shared__ __align__(8) uint64_t q_full[2], q_empty[2];
+    __shared__ __align__(8) uint64_t ring_full[C::RING], ring_empty[C::RING];
+    __shared__ __align__(8) uint64_t s_full[2], s_free[2], pv_done[2];
+    __shared__ __align__(8) uint64_t o_full[2], o_free[2];
     __shared__ __align__(8) uint64_t drain;
+    __shared__ int item_sh[kItemSlots];
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
@@ -80,36 +128,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
-    const AttnItem item = p.items[blockIdx.x];
-    const bool two = item.qt1 >= 0;
-    const int kvh = item.h0 / (p.n_heads / p.n_kv_heads);
-    const int seq0 = p.offsets[item.seq];
-    const int L = p.offsets[item.seq + 1] - seq0;
-    const int qt_max = two ? max(item.qt0, item.qt1) : item.qt0;
-    const int kend = p.causal ? min(qt_max * kTile + kTile, L) : L;
-    const int n_kt = (kend + kKT - 1) / kKT;
-
     if (threadIdx.x == 0) {
-        mbar_init(&q_full, 1);
-        for (int i = 0; i < kRingSlots; ++i) {
+        for (int i = 0; i < kItemSlots; ++i) mbar_init(&item_full[i], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&q_full[b], 1);
+            mbar_init(&q_empty[b], 1);
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_free[b], 4);
+            mbar_init(&pv_done[b], 1);
+            mbar_init(&o_full[b], 1);
+            mbar_init(&o_free[b], 4);
+        }
+        for (int i = 0; i < C::RING; ++i) {
             mbar_init(&ring_full[i], 1);
             mbar_init(&ring_empty[i], 1);
         }
-        for (int w = 0; w < 2; ++w)
-            for (int b = 0; b < 2; ++b) {
-                mbar_init(&s_full[w][b], 1);
-                mbar_init(&s_free[w][b], 4);
-                mbar_init(&p_full[w][b], 4);
-                mbar_init(&pv_done[w][b], 1);
-            }
         mbar_init(&drain, 1);
         abort_sh = 0;
         fence_barrier_init();
     }
-    if (warp == kProducerWarp && lane == 0) {
-        tma_prefetch_desc(&tmq);
-        tma_prefetch_desc(&tmkv);
-    }
+    if (warp == kProducerWarp && lane == 0) tma_prefetch_desc(&tm);
     if (warp == kMmaWarp) {
         tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
         tmem_relinquish();
@@ -125,123 +163,173 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (warp == kProducerWarp) {
         if (lane == 0) {
             // ------------------------------------------------------------ producer
-            int issued = 0;
+            int e = 0;  // ring entry counter: K(g) is entry 2g, V(g) entry 2g + 1
+            int k = 0;  // CTA-local item counter
+            int q_issued = 0;
             bool ok = true;
-            mbar_arrive_expect_tx(&q_full, (two ? 2 : 1) * C::Q_BYTES);
-            for (int b = 0; b < C::NBOX; ++b)
-                tma_load_2d(sQ + b * C::QBOX, &tmq, &q_full, p.q_col0 + item.h0 * D + b * C::BOXC,
-                            seq0 + item.qt0 * kTile);
-            if (two)
-                for (int b = 0; b < C::NBOX; ++b)
-                    tma_load_2d(sQ + C::Q_BYTES + b * C::QBOX, &tmq, &q_full,
-                                p.q_col0 + item.h1 * D + b * C::BOXC, seq0 + item.qt1 * kTile);
-            for (int i = 0; i < 2 * n_kt; ++i) {
-                const int slot = i % kRingSlots;
-                const uint32_t ph = (i / kRingSlots) & 1;
-                if (!mbar_wait(&ring_empty[slot], ph ^ 1, p.err, &abort_sh)) {
+            for (;; ++k) {
+                int idx = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.sched, 1);
+                if (idx >= p.n_items) idx = -1;
+                // Entry k % 4 was last read for item k - 4; every role has started
+                // item k - 3 by now (the Q wait below for item k - 1 passed), so it
+                // is free.
+                item_sh[k % kItemSlots] = idx;
+                mbar_arrive(&item_full[k % kItemSlots]);
+                if (idx < 0) break;
+                const ItemGeo g = item_geo(p, idx);
+                const int qb = k & 1;
+                if (!mbar_wait(&q_empty[qb], ((k >> 1) & 1) ^ 1, p.err, &abort_sh)) {
                     ok = false;
                     break;
                 }
-                const int col = ((i & 1) ? p.v_col0 : p.k_col0) + kvh * D;
-                const int row = seq0 + (i >> 1) * kKT;
-                mbar_arrive_expect_tx(&ring_full[slot], C::KV_BYTES);
-                for (int b = 0; b < C::NBOX; ++b)
-                    tma_load_2d(sRing + slot * C::KV_BYTES + b * C::KVBOX, &tmkv, &ring_full[slot],
-                                col + b * C::BOXC, row);
-                ++issued;
+                mbar_arrive_expect_tx(&q_full[qb], 2 * C::TILE_BYTES);
+                for (int blk = 0; blk < 2; ++blk)
+                    for (int bx = 0; bx < C::NBOX; ++bx)
+                        tma_load_2d(sQ + (qb * 2 + blk) * C::TILE_BYTES + bx * C::BOX_BYTES, &tm,
+                                    &q_full[qb], p.q_col0 + g.h[blk] * D + bx * C::BOXC,
+                                    g.seq0 + g.qt[blk] * kTile);
+                q_issued = k + 1;
+                for (int t = 0; t < 2 * g.n_kt; ++t, ++e) {
+                    const int slot = e % C::RING;
+                    if (!mbar_wait(&ring_empty[slot], ((e / C::RING) & 1) ^ 1, p.err,
+                                   &abort_sh)) {
+                        ok = false;
+                        break;
+                    }
+                    const int col = ((t & 1) ? p.v_col0 : p.k_col0) + g.kvh * D;
+                    const int row = g.seq0 + (t >> 1) * kTile;
+                    mbar_arrive_expect_tx(&ring_full[slot], C::TILE_BYTES);
+                    for (int bx = 0; bx < C::NBOX; ++bx)
+                        tma_load_2d(sRing + slot * C::TILE_BYTES + bx * C::BOX_BYTES, &tm,
+                                    &ring_full[slot], col + bx * C::BOXC, row);
+                }
+                if (!ok) break;
             }
-            if (!ok) {
-                mbar_wait(&q_full, 0, nullptr, nullptr);
-                for (int i = issued - kRingSlots < 0 ? 0 : issued - kRingSlots; i < issued; ++i)
-                    mbar_wait(&ring_full[i % kRingSlots], (i / kRingSlots) & 1, nullptr, nullptr);
+            if (!ok) {  // let loads in flight land before the CTA exits
+                for (int j = e - C::RING < 0 ? 0 : e - C::RING; j < e; ++j)
+                    mbar_wait(&ring_full[j % C::RING], (j / C::RING) & 1, nullptr, nullptr);
+                for (int j = q_issued - 2 < 0 ? 0 : q_issued - 2; j < q_issued; ++j)
+                    mbar_wait(&q_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
             }
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
-            constexpr uint32_t IDESC_S = idesc_f16(128, kKT, 1, 1, 0, 0);
+            constexpr uint32_t IDESC_S = idesc_f16(128, kTile, 1, 1, 0, 0);
             constexpr uint32_t IDESC_O = idesc_f16(128, D, 1, 1, 0, 1);
-            const int nw = two ? 2 : 1;
-            // Descriptors are linear in the start address (16-byte units in the
-            // low bits): each operand's descriptor is built once and offset.
-            const uint64_t dQ = kmajor_desc<D>(smem_u32(sQ));
-            const uint64_t dRingK = kmajor_desc<D>(smem_u32(sRing));
-            const uint64_t dRingV = smem_desc(smem_u32(sRing), C::KVBOX, C::SBO, C::LAYOUT);
+            const uint64_t dQ = smem_desc(smem_u32(sQ), 16, C::SBO, C::LAYOUT);
+            const uint64_t dRingK = smem_desc(smem_u32(sRing), 16, C::SBO, C::LAYOUT);
+            const uint64_t dRingV = smem_desc(smem_u32(sRing), C::BOX_BYTES, C::SBO, C::LAYOUT);
             auto kk_off = [](int kk) -> uint64_t {  // K-major k-step offset (16-byte units)
                 const int e = kk * 16;
-                return (uint64_t)(((e / C::BOXC) * C::QBOX + (e % C::BOXC) * 2) >> 4);
+                return (uint64_t)(((e / C::BOXC) * C::BOX_BYTES + (e % C::BOXC) * 2) >> 4);
             };
-            auto kk_offk = [](int kk) -> uint64_t {
-                const int e = kk * 16;
-                return (uint64_t)(((e / C::BOXC) * C::KVBOX + (e % C::BOXC) * 2) >> 4);
+            auto wait_ring = [&](int e) -> bool {
+                return mbar_wait(&ring_full[e % C::RING], (e / C::RING) & 1, p.err, &abort_sh);
             };
-            auto wait_slot = [&](int i) -> bool {
-                return mbar_wait(&ring_full[i % kRingSlots], (i / kRingSlots) & 1, p.err, &abort_sh);
+            // Next item: its tile count, or 0 at the end of the list (or on failure).
+            auto next_item = [&](int k, bool &ok) -> int {
+                if (!mbar_wait(&item_full[k % kItemSlots], (k / kItemSlots) & 1, p.err,
+                               &abort_sh)) {
+                    ok = false;
+                    return 0;
+                }
+                const int idx = item_sh[k % kItemSlots];
+                return idx < 0 ? 0 : item_geo(p, idx).n_kt;
             };
-            auto issue_s = [&](int w, int j) {
-                const uint64_t dK = dRingK + (uint64_t)((((2 * j) % kRingSlots) * C::KV_BYTES) >> 4);
-                const uint64_t dQw = dQ + (uint64_t)((w * C::Q_BYTES) >> 4);
-                const uint32_t d = tmem_base + 256 + (2 * w + (j & 1)) * kKT;
+            // S_b(g) for block b of item k (Q buffer k & 1) against K(g).
+            auto issue_s = [&](int b, int k, int g) {
+                const uint64_t dK = dRingK + (uint64_t)((((2 * g) % C::RING) * C::TILE_BYTES) >> 4);
+                const uint64_t dQb = dQ + (uint64_t)((((k & 1) * 2 + b) * C::TILE_BYTES) >> 4);
+                const uint32_t d = tmem_base + b * kTile;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(d, dQw + kk_off(kk), dK + kk_offk(kk), IDESC_S, kk != 0);
+                    umma_f16(d, dQb + kk_off(kk), dK + kk_off(kk), IDESC_S, kk != 0);
+                umma_commit(&s_full[b]);
             };
-            auto issue_pv = [&](int w, int j) {
-                const uint64_t dV =
-                    dRingV + (uint64_t)((((2 * j + 1) % kRingSlots) * C::KV_BYTES) >> 4);
-                const uint32_t tP = tmem_base + 256 + (2 * w + (j & 1)) * kKT;
-                const uint32_t d = tmem_base + w * D;
-#pragma unroll
-                for (int kk = 0; kk < kKT / 16; ++kk)
-                    umma_f16_ts(d, tP + kk * 8, dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O,
-                                (j | kk) != 0);
-            };
-            bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh);
-            // Prologue: S(0) and S(1) for both blocks.
-            for (int j = 0; ok && j < 2 && j < n_kt; ++j) {
-                if (!wait_slot(2 * j)) {
+            bool ok = true;
+            int k = 0, g = 0;  // local item, global tile counter
+            int n = next_item(0, ok);
+            // First item's S0(0), S1(0).
+            if (n > 0) {
+                if (!mbar_wait(&q_full[0], 0, p.err, &abort_sh) || !wait_ring(0)) {
                     ok = false;
-                    break;
+                    n = 0;
+                } else {
+                    tc_fence_after();
+                    issue_s(0, 0, 0);
+                    issue_s(1, 0, 0);
+                    umma_commit(&ring_empty[0]);
+                    if (n == 1) umma_commit(&q_empty[0]);
                 }
-                tc_fence_after();
-                for (int w = 0; w < nw; ++w) {
-                    issue_s(w, j);
-                    umma_commit(&s_full[w][j & 1]);
-                }
-                umma_commit(&ring_empty[(2 * j) % kRingSlots]);
             }
-            for (int j = 0; ok && j < n_kt; ++j) {
-                const int b = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                const bool more = j + 2 < n_kt;
-                if (!wait_slot(2 * j + 1)) {
-                    ok = false;
-                    break;
-                }
-                for (int w = 0; w < nw && ok; ++w) {
-                    if (!mbar_wait(&p_full[w][b], ph, p.err, &abort_sh)) {
+            while (ok && n > 0) {
+                int n_next = -1;  // tile count of item k + 1 once fetched
+                for (int j = 0; ok && j < n; ++j, ++g) {
+                    if (!wait_ring(2 * g + 1)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    issue_pv(w, j);
-                    umma_commit(&pv_done[w][b]);
-                    if (more) {
-                        // S_w(j+2) reuses S buffer b once the softmax has read S_w(j).
-                        if (!mbar_wait(&s_free[w][b], ph, p.err, &abort_sh) ||
-                            (w == 0 && !wait_slot(2 * j + 4))) {
+                    const uint64_t dV =
+                        dRingV + (uint64_t)((((2 * g + 1) % C::RING) * C::TILE_BYTES) >> 4);
+                    for (int b = 0; b < 2; ++b) {
+                        // PV_b(g): P_b(g) written, O_b free at an item's first tile.
+                        if (!mbar_wait(&s_free[b], g & 1, p.err, &abort_sh) ||
+                            (j == 0 &&
+                             !mbar_wait(&o_free[b], (k & 1) ^ 1, p.err, &abort_sh))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        issue_s(w, j + 2);
-                        umma_commit(&s_full[w][b]);
+                        const uint32_t tP = tmem_base + b * kTile;
+                        const uint32_t dO = tmem_base + 256 + b * 128;
+#pragma unroll
+                        for (int kk = 0; kk < kTile / 16; ++kk)
+                            umma_f16_ts(dO, tP + kk * 8,
+                                        dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O,
+                                        (j | kk) != 0);
+                        umma_commit(&pv_done[b]);
+                        if (j == n - 1) umma_commit(&o_full[b]);
+                        if (b == 1) umma_commit(&ring_empty[(2 * g + 1) % C::RING]);
+                        // Next S of block b: tile j + 1 of this item, or tile 0 of the next.
+                        if (j + 1 < n) {
+                            if (b == 0 && !wait_ring(2 * g + 2)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_s(b, k, g + 1);
+                            if (b == 1) {
+                                umma_commit(&ring_empty[(2 * g + 2) % C::RING]);
+                                if (j + 2 == n) umma_commit(&q_empty[k & 1]);
+                            }
+                        } else {
+                            if (b == 0) {
+                                n_next = next_item(k + 1, ok);
+                                if (n_next > 0 &&
+                                    (!mbar_wait(&q_full[(k + 1) & 1], ((k + 1) >> 1) & 1, p.err,
+                                                &abort_sh) ||
+                                     !wait_ring(2 * g + 2))) {
+                                    ok = false;
+                                    n_next = 0;
+                                }
+                                if (!ok) break;
+                            }
+                            if (n_next > 0) {
+                                tc_fence_after();
+                                issue_s(b, k + 1, g + 1);
+                                if (b == 1) {
+                                    umma_commit(&ring_empty[(2 * g + 2) % C::RING]);
+                                    if (n_next == 1) umma_commit(&q_empty[(k + 1) & 1]);
+                                }
+                            }
+                        }
                     }
                 }
                 if (!ok) break;
-                umma_commit(&ring_empty[(2 * j + 1) % kRingSlots]);
-                if (more) umma_commit(&ring_empty[(2 * j + 4) % kRingSlots]);
+                ++k;
+                n = n_next;
             }
             if (!ok) {
                 umma_commit(&drain);
@@ -251,62 +339,65 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
     } else if (warp < 8) {
         // ---------------------------------------------------------------- softmax
-        const int w = warp >> 2;
-        if (w == 0 || two) {
-            const int quad = warp & 3;
-            const int r = quad * 32 + lane;
-            const int qt = w == 0 ? item.qt0 : item.qt1;
-            const int h = w == 0 ? item.h0 : item.h1;
-            const int q = qt * kTile + r;
-            const float sl2 = p.scale * 1.4426950408889634f;
-            const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-            const uint32_t tO = tmem_base + lane_off + w * D;
+        const int b = warp >> 2;
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const float sl2 = p.scale * 1.4426950408889634f;
+        const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+        const uint32_t tS = tmem_base + lane_off + b * kTile;
+        const uint32_t tO = tmem_base + lane_off + 256 + b * 128;
+        int g = 0;
+        for (int k = 0;; ++k) {
+            if (!mbar_wait(&item_full[k % kItemSlots], (k / kItemSlots) & 1, p.err, &abort_sh))
+                break;
+            const int idx = item_sh[k % kItemSlots];
+            if (idx < 0) break;
+            const ItemGeo it = item_geo(p, idx);
+            const int q = it.qt[b] * kTile + r;
             float m_used = -INFINITY, l = 0.0f;
             bool ok = true;
-            for (int j = 0; j < n_kt; ++j) {
-                const int b = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&s_full[w][b], ph, p.err, &abort_sh)) {
+            for (int j = 0; j < it.n_kt; ++j, ++g) {
+                if (!mbar_wait(&s_full[b], g & 1, p.err, &abort_sh)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t tS = tmem_base + lane_off + 256 + (2 * w + b) * kKT;
-                float v0[32], v1[32];
-                tmem_ld32(tS, v0);
-                tmem_ld32(tS + 32, v1);
+                float s[kTile];
+                tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
+                tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+                tmem_ld32(tS + 64, *reinterpret_cast<float(*)[32]>(&s[64]));
+                tmem_ld32(tS + 96, *reinterpret_cast<float(*)[32]>(&s[96]));
                 tmem_wait_ld();
-#define V(i) ((i) < 32 ? v0[(i)] : v1[(i) - 32])
-                const int k0 = j * kKT;
-                // Tiles wholly inside the sequence and below the diagonal need no mask.
-                if (k0 + kKT > L || (p.causal && k0 + kKT - 1 > qt * kTile)) {
+                const int k0 = j * kTile;
+                const int vis = p.causal ? min(it.L - k0, q - k0 + 1) : it.L - k0;
+                if (vis < kTile) {
 #pragma unroll
-                    for (int i = 0; i < kKT; ++i) {
-                        const int key = k0 + i;
-                        if (!(key < L && (!p.causal || key <= q))) V(i) = -INFINITY;
-                    }
+                    for (int i = 0; i < kTile; ++i) s[i] = i < vis ? s[i] : -INFINITY;
                 }
-                float mxa[8];
+                float mx[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) mxa[i] = V(i);
+                for (int u = 0; u < 4; ++u) mx[u] = max3(s[u], s[4 + u], s[8 + u]);
 #pragma unroll
-                for (int i = 8; i < kKT; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], V(i));
-                const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-                const float m_new = fmaxf(m_used, mx * sl2);
+                for (int i = 12; i + 8 <= kTile; i += 8)
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) mx[u] = max3(mx[u], s[i + u], s[i + 4 + u]);
+                mx[0] = max3(mx[0], mx[1], s[kTile - 4]);
+                mx[2] = max3(mx[2], mx[3], s[kTile - 3]);
+                const float rmax = max3(mx[0], mx[2], fmaxf(s[kTile - 2], s[kTile - 1]));
+                const float m_new = fmaxf(m_used, rmax * sl2);
                 if (j == 0) {
                     m_used = m_new;
                 } else if (__any_sync(0xffffffffu, m_new > m_used + kRescaleLog2)) {
-                    // O_w may only change once PV_w(j-1) has completed; PV_w(j)
-                    // waits for this block's P_w(j).
-                    if (!mbar_wait(&pv_done[w][(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, &abort_sh)) {
+                    // O may change only once PV_b(g - 1) has completed; PV_b(g)
+                    // waits for this tile's P.
+                    if (!mbar_wait(&pv_done[b], (g - 1) & 1, p.err, &abort_sh)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const float alpha = ex2_approx(m_used - m_new);
 #pragma unroll 1
-                    for (int c = 0; c < D / 32; ++c) {
+                    for (int c = 0; c < D / C::CW; ++c) {
                         float o[32];
                         tmem_ld32(tO + c * 32, o);
                         tmem_wait_ld();
@@ -318,49 +409,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     l *= alpha;
                     m_used = m_new;
                 }
-                // P_w(j) overwrites the S_w(j) columns just read (P_w(j-2) in the
-                // other buffer may still be in use by PV_w(j-2)).
-                uint32_t pk[32];
+                // P over the first 64 columns of the score buffer: key 2c, 2c + 1 in
+                // column c.  Every eighth pair goes through the FMA-pipe exp2.
                 float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float p0 = ex2_approx(fmaf(V(2 * i), sl2, -m_used));
-                    const float p1 = ex2_approx(fmaf(V(2 * i + 1), sl2, -m_used));
-                    la[i & 3] += p0 + p1;
-                    pk[i] = pack_bf16x2(p0, p1);
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int e0 = h * 64 + 2 * i;
+                        const float x0 = fmaf(s[e0], sl2, -m_used);
+                        const float x1 = fmaf(s[e0 + 1], sl2, -m_used);
+                        float p0, p1;
+                        if ((i & 3) == 3) {
+                            p0 = exp2_fma(x0);
+                            p1 = exp2_fma(x1);
+                        } else {
+                            p0 = ex2_approx(x0);
+                            p1 = ex2_approx(x1);
+                        }
+                        la[i & 3] += p0 + p1;
+                        pk[i] = pack_bf16x2(p0, p1);
+                    }
+                    tmem_st32u(tS + h * 32, pk);
                 }
-#undef V
-                tmem_st32u(tS, pk);
                 tmem_wait_st();
                 l += (la[0] + la[1]) + (la[2] + la[3]);
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&s_free[w][b]);
-                    mbar_arrive(&p_full[w][b]);
-                }
+                if (lane == 0) mbar_arrive(&s_free[b]);
             }
-            const int jl = n_kt - 1;
-            if (ok && mbar_wait(&pv_done[w][jl & 1], (jl >> 1) & 1, p.err, &abort_sh)) {
-                tc_fence_after();
-                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-                __nv_bfloat16 *orow = p.out + (size_t)(seq0 + q) * p.ldo + h * D;
+            if (!ok) break;
+            // Item done: write O / l, release O_b.
+            if (!mbar_wait(&o_full[b], k & 1, p.err, &abort_sh)) break;
+            tc_fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const bool store = q < it.L && (b == 0 || it.store1);
+            __nv_bfloat16 *orow = p.out + (size_t)(it.seq0 + q) * p.ldo + it.h[b] * D;
 #pragma unroll 1
-                for (int c = 0; c < D / 32; ++c) {
-                    float o[32];
+            for (int c = 0; c < D / C::CW; ++c) {
+                float o[C::CW];
+                if constexpr (C::CW == 32)
                     tmem_ld32(tO + c * 32, o);
-                    tmem_wait_ld();
-                    if (q < L) {
-                        uint4 *op = reinterpret_cast<uint4 *>(orow + c * 32);
+                else
+                    tmem_ld16(tO + c * 16, o);
+                tmem_wait_ld();
+                if (store) {
+                    uint4 *op = reinterpret_cast<uint4 *>(orow + c * C::CW);
 #pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
-                                               pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
-                                               pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
-                                               pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
-                    }
+                    for (int u = 0; u < C::CW / 8; ++u)
+                        op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
+                                           pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
+                                           pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
+                                           pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free[b]);
         }
     }
 
@@ -369,6 +475,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+    // The last CTA to finish rewinds the claim counter for the next launch.
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+            atomicExch(p.sched, 0);
+            atomicExch(p.sched + 1, 0);
+        }
     }
 }
 
@@ -461,26 +575,28 @@ __global__ void __launch_bounds__(kF32Threads)
 
 }  // namespace
 
-int attention_tc_launch(const CUtensorMap *q_map, const CUtensorMap *kv_map, const AttnParams &p,
-                        cudaStream_t stream) {
+int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStream_t stream) {
     if (p.n_items <= 0) return cudaSuccess;
-    dim3 grid(p.n_items);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    dim3 grid(p.n_items < sms ? p.n_items : sms);  // persistent
     cudaError_t e;
     switch (p.head_dim) {
     case 32:
         e = set_smem_once<attn_tc_kernel<32>>(AttnCfg<32>::SMEM);
         if (e != cudaSuccess) return e;
-        attn_tc_kernel<32><<<grid, kAttnThreads, AttnCfg<32>::SMEM, stream>>>(*q_map, *kv_map, p);
+        attn_tc_kernel<32><<<grid, kAttnThreads, AttnCfg<32>::SMEM, stream>>>(*qkv_map, p);
         break;
     case 64:
         e = set_smem_once<attn_tc_kernel<64>>(AttnCfg<64>::SMEM);
         if (e != cudaSuccess) return e;
-        attn_tc_kernel<64><<<grid, kAttnThreads, AttnCfg<64>::SMEM, stream>>>(*q_map, *kv_map, p);
+        attn_tc_kernel<64><<<grid, kAttnThreads, AttnCfg<64>::SMEM, stream>>>(*qkv_map, p);
         break;
     case 128:
         e = set_smem_once<attn_tc_kernel<128>>(AttnCfg<128>::SMEM);
         if (e != cudaSuccess) return e;
-        attn_tc_kernel<128><<<grid, kAttnThreads, AttnCfg<128>::SMEM, stream>>>(*q_map, *kv_map, p);
+        attn_tc_kernel<128><<<grid, kAttnThreads, AttnCfg<128>::SMEM, stream>>>(*qkv_map, p);
         break;
     default:
         return cudaErrorInvalidValue;
@@ -516,9 +632,9 @@ int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, co
         const int L = h_offsets[b + 1] - h_offsets[b];
         if (!tc) {
             n += ceil_div(L, attention_f32_qtile(head_dim));
-        } else if (rep >= 2) {
+        } else if (rep >= 2) {  // head pairs of each key/value head
             n += (long long)ceil_div(L, kTile) * n_kv_heads * ceil_div(rep, 2);
-        } else {
+        } else {  // query-tile pairs of each head
             n += (long long)ceil_div(ceil_div(L, kTile), 2) * n_heads;
         }
     }
@@ -534,46 +650,49 @@ int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int 
         out[n++] = it;
         return true;
     };
-    for (int b = 0; b < batch; ++b) {
-        const int L = h_offsets[b + 1] - h_offsets[b];
-        if (!tc) {
+    if (!tc) {
+        for (int b = 0; b < batch; ++b) {
+            const int L = h_offsets[b + 1] - h_offsets[b];
             const int qt = attention_f32_qtile(head_dim);
             const int nq = ceil_div(L, qt);
             for (int t = 0; t < nq; ++t)
                 if (!push(AttnItem{b, t, -1, -1, -1, causal ? t + 1 : nq})) return -1;
-            continue;
         }
+        std::stable_sort(out, out + n, [](const AttnItem &x, const AttnItem &y) {
+            return x.cost > y.cost;
+        });
+        return n;
+    }
+    // Sequences longest first; within a sequence the items of one key/value head
+    // (or head) stay together, heaviest query tile first, so the CTAs working at
+    // the same time read the same keys and values.
+    std::vector<int> order(batch);
+    for (int b = 0; b < batch; ++b) order[b] = b;
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+        return h_offsets[x + 1] - h_offsets[x] > h_offsets[y + 1] - h_offsets[y];
+    });
+    for (int b : order) {
+        const int L = h_offsets[b + 1] - h_offsets[b];
         const int nq = ceil_div(L, kTile);
         if (rep >= 2) {
-            // Two q-heads of one kv head share every K/V tile.
-            for (int t = 0; t < nq; ++t)
-                for (int g = 0; g < n_kv_heads; ++g)
-                    for (int pr = 0; pr < rep; pr += 2) {
-                        const int h0 = g * rep + pr;
-                        const bool has1 = pr + 1 < rep;
-                        const int kt = causal ? t + 1 : nq;
-                        if (!push(AttnItem{b, t, h0, has1 ? t : -1, has1 ? h0 + 1 : -1,
-                                           kt * (has1 ? 2 : 1)}))
+            for (int kvh = 0; kvh < n_kv_heads; ++kvh)
+                for (int t = nq - 1; t >= 0; --t)
+                    for (int h = kvh * rep; h < (kvh + 1) * rep; h += 2) {
+                        const bool pair = h + 1 < (kvh + 1) * rep;
+                        if (!push(AttnItem{b, t, h, pair ? t : -1, pair ? h + 1 : -1,
+                                           causal ? t + 1 : nq}))
                             return -1;
                     }
         } else {
-            // Full multi-head: two query tiles of one head share the K/V stream.
             for (int h = 0; h < n_heads; ++h)
-                for (int t = 0; t < nq; t += 2) {
-                    const bool has1 = t + 1 < nq;
-                    const int kt = causal ? (has1 ? t + 2 : t + 1) : nq;
-                    if (!push(AttnItem{b, t, h, has1 ? t + 1 : -1, has1 ? h : -1,
-                                       kt * (has1 ? 2 : 1)}))
+                for (int t = nq - 1; t >= 0; t -= 2) {
+                    const bool pair = t >= 1;
+                    if (!push(AttnItem{b, pair ? t - 1 : t, h, pair ? t : -1, pair ? h : -1,
+                                       causal ? t + 1 : nq}))
                         return -1;
                 }
         }
     }
-    std::sort(out, out + n, [](const AttnItem &x, const AttnItem &y) {
-        if (x.cost != y.cost) return x.cost > y.cost;
-        if (x.seq != y.seq) return x.seq < y.seq;
-        if (x.qt0 != y.qt0) return x.qt0 < y.qt0;
-        return x.h0 < y.h0;
-    });
     return n;
 }
 

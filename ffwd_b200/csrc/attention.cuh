@@ -16,10 +16,10 @@
 
 namespace fb {
 
-// One work item of a CTA.  Tensor-core path: up to two query blocks
-// (query tile, head) that share one key/value head, processed by the CTA's two
-// softmax warpgroups over one stream of K/V tiles; qt1 = -1 when the second
-// block is absent.  f32 path: (seq, qt0) with the head taken from blockIdx.y.
+// One work item.  Tensor-core path: two query blocks of 128 rows that share
+// their keys and values, block 0 = (query tile qt0, head h0), block 1 = (qt1,
+// h1); qt1 = h1 = -1 when the item has block 0 only.  f32 path: (seq, qt0)
+// with the head taken from blockIdx.y; qt1 / h1 unused (-1).
 struct AttnItem {
     int seq;
     int qt0, h0;
@@ -44,23 +44,27 @@ struct AttnParams {
     __nv_bfloat16 *out_hi;  // split output (hi / lo) for the next 2- or 3-pass GEMM
     __nv_bfloat16 *out_lo;
     int *err;
+    int *sched;             // tensor-core path: 2 ints (claim counter, exit count), zero
+                            // before the first launch; the kernel rewinds them on exit
 };
 
 // Build the work list of a packed batch (host).  tc selects the tensor-core
-// pairing (128-row query tiles, two blocks per item) or the f32 path's items.
-// Writes at most cap items to out, sorted heaviest first (ties in a fixed
-// order); returns the count, or -1 if cap is too small.  Allocates nothing.
+// items (pairs of 128-row query blocks sharing a key/value head: two query
+// heads of a group, or two adjacent query tiles when every head has its own
+// key/value head), ordered longest sequence first with the items of one
+// key/value head together; or the f32 path's items, heaviest first.
+// Writes at most cap items to out; returns the count, or -1 if cap is too
+// small.  Allocates nothing beyond a sequence order of `batch` ints.
 int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int head_dim,
                           const int *h_offsets, int batch, AttnItem *out, int cap);
 // Number of items attention_build_items would write.
 int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, const int *h_offsets,
                           int batch);
 
-// Tensor-core path.  `q_map` / `kv_map`: 2-D bf16 maps over the qkv matrix
-// with boxes of 128 / 64 rows x min(head_dim, 64) columns (128-byte swizzle, or
-// 64-byte for head_dim 32).
-int attention_tc_launch(const CUtensorMap *q_map, const CUtensorMap *kv_map, const AttnParams &p,
-                        cudaStream_t stream);
+// Tensor-core path.  `qkv_map`: 2-D bf16 map over the qkv matrix with a box of
+// 128 rows x min(head_dim, 64) columns (128-byte swizzle, or 64-byte for
+// head_dim 32).
+int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStream_t stream);
 
 // f32 CUDA-core path for the exact (f32 / split-bf16) precision mode.  Items
 // here use query tiles of attention_f32_qtile(head_dim) rows.

@@ -585,7 +585,9 @@ int ensure_ws(ffwd_b200_ctx *ctx, Device &D, int T, int B, int n_items, int n_sp
         w.cap_spans = cap;
     }
     if (!w.err) {
-        CK(cudaMalloc(&w.err, 4));
+        // err[0]: device error word; err[2..3]: attention scheduler counters.
+        CK(cudaMalloc(&w.err, 16));
+        CK(cudaMemset(w.err, 0, 16));
         CK(cudaMallocHost(&w.h_err, 4));
     }
     return 0;
@@ -693,6 +695,7 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
     ap.out_hi = w.att;
     ap.out_lo = w.att_lo;
     ap.err = w.err;
+    ap.sched = w.err + 2;
 
     const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
     LAUNCH((positions_kernel<<<B, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0, w.pos),
@@ -748,7 +751,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
         if (split)
             LAUNCH(attention_f32_launch(fs.ap, s));
         else
-            LAUNCH(attention_tc_launch(&fs.m_qkv, &fs.m_kv, fs.ap, s));
+            LAUNCH(attention_tc_launch(&fs.m_qkv, fs.ap, s));
         return 0;
     case kOpO: {  // output projection + residual (+ bias)
         GemmParams p{};
@@ -1429,7 +1432,7 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     const int H = c.hidden_size, I = c.intermediate_size, qkv_dim = c.q_dim + 2 * c.kv_dim;
     Workspace w{};
     Carver cv{base, 0, kNoAllocScratchBytes};
-    bool ok = cv.take(&w.err, 1) && cv.take(&w.offsets, (size_t)batch + 1) &&
+    bool ok = cv.take(&w.err, 4) && cv.take(&w.offsets, (size_t)batch + 1) &&
               cv.take(&w.items, (size_t)n_items) && cv.take(&w.ids, (size_t)T) &&
               cv.take(&w.pos, (size_t)T) && cv.take(&w.x, (size_t)T * H) &&
               cv.take(&w.xb, (size_t)T * H) && cv.take(&w.att, (size_t)T * c.q_dim) &&
@@ -1452,7 +1455,7 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     w.cap_items = n_items;
 
     cudaStream_t s = D.stream;
-    CK(cudaMemsetAsync(w.err, 0, 4, s));  // the arena keeps the previous call's error word
+    CK(cudaMemsetAsync(w.err, 0, 16, s));  // error word and scheduler counters
     CK(cudaMemcpyAsync(w.ids, d_ids, (size_t)T * 4, cudaMemcpyDeviceToDevice, s));
     CK(cudaMemcpyAsync(w.offsets, h_offsets, (size_t)(batch + 1) * 4, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(w.items, items, (size_t)n_items * sizeof(AttnItem), cudaMemcpyHostToDevice,
@@ -1497,6 +1500,7 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     ap.out_hi = w.att;
     ap.out_lo = w.att_lo;
     ap.err = w.err;
+    ap.sched = w.err + 2;
 
     const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
     LAUNCH((positions_kernel<<<batch, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0,
