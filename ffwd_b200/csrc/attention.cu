@@ -7,7 +7,7 @@
 // both blocks, which halves the K/V traffic.  CTAs claim items in list order
 // from a global counter; the list keeps the items of one (sequence, key/value
 // head) together, so CTAs that run at the same time share K/V in L2.
-// 384 threads:
+// 320 threads:
 //   warps 0-3   softmax of block 0, warps 4-7 block 1: one thread per query
 //               row reads its 128 scores from TMEM, masks (length, causal),
 //               writes P = exp2(s - m) as packed bf16 over the first half of
@@ -37,7 +37,7 @@ namespace fb {
 namespace {
 
 constexpr int kTile = 128;  // query rows per block and keys per key tile
-constexpr int kAttnThreads = 384;
+constexpr int kAttnThreads = 320;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kItemSlots = 4;  // published-item ring
@@ -87,7 +87,7 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // Item geometry, recomputed by every role from the shared work list.
 struct ItemGeo {
     int seq0, L, kvh, n_kt;
-    int qt[2], h[2];
+    int qt0, h0, qt1, h1;
     bool store1;  // block 1 is a real block (else it repeats block 0, unstored)
 };
 
@@ -97,12 +97,12 @@ __device__ __forceinline__ ItemGeo item_geo(const AttnParams &p, int idx) {
     g.seq0 = p.offsets[it.seq];
     g.L = p.offsets[it.seq + 1] - g.seq0;
     g.store1 = it.qt1 >= 0;
-    g.qt[0] = it.qt0;
-    g.h[0] = it.h0;
-    g.qt[1] = g.store1 ? it.qt1 : it.qt0;
-    g.h[1] = g.store1 ? it.h1 : it.h0;
+    g.qt0 = it.qt0;
+    g.h0 = it.h0;
+    g.qt1 = g.store1 ? it.qt1 : it.qt0;
+    g.h1 = g.store1 ? it.h1 : it.h0;
     g.kvh = it.h0 / (p.n_heads / p.n_kv_heads);
-    const int qmax = max(g.qt[0], g.qt[1]);
+    const int qmax = max(g.qt0, g.qt1);
     const int kend = p.causal ? min(qmax * kTile + kTile, g.L) : g.L;
     g.n_kt = (kend + kTile - 1) / kTile;
     return g;
@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __shared__ __align__(8) uint64_t item_full[kItemSlots];
     __shared__ __align__(8) uint64_t q_full[2], q_empty[2];
     __shared__ __align__(8) uint64_t ring_full[C::RING], ring_empty[C::RING];
-    __shared__ __align__(8) uint64_t s_full[2], s_free[2], pv_done[2];
+    __shared__ __align__(8) uint64_t s_full[2], s_free[2];
     __shared__ __align__(8) uint64_t o_full[2], o_free[2];
     __shared__ __align__(8) uint64_t drain;
     __shared__ int item_sh[kItemSlots];
@@ -135,7 +135,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             mbar_init(&q_empty[b], 1);
             mbar_init(&s_full[b], 1);
             mbar_init(&s_free[b], 4);
-            mbar_init(&pv_done[b], 1);
             mbar_init(&o_full[b], 1);
             mbar_init(&o_free[b], 4);
         }
@@ -186,8 +185,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 for (int blk = 0; blk < 2; ++blk)
                     for (int bx = 0; bx < C::NBOX; ++bx)
                         tma_load_2d(sQ + (qb * 2 + blk) * C::TILE_BYTES + bx * C::BOX_BYTES, &tm,
-                                    &q_full[qb], p.q_col0 + g.h[blk] * D + bx * C::BOXC,
-                                    g.seq0 + g.qt[blk] * kTile);
+                                    &q_full[qb], p.q_col0 + (blk ? g.h1 : g.h0) * D + bx * C::BOXC,
+                                    g.seq0 + (blk ? g.qt1 : g.qt0) * kTile);
                 q_issued = k + 1;
                 for (int t = 0; t < 2 * g.n_kt; ++t, ++e) {
                     const int slot = e % C::RING;
@@ -216,6 +215,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
+            // Issuing costs this thread about as long as the tensor pipe takes
+            // to execute a 128 x 128 x 16 MMA, and a satisfied barrier wait
+            // several times that, so the barrier of the next step is probed
+            // (non-blocking) before the current MMAs are issued and only
+            // waited on when the probe failed.
             constexpr uint32_t IDESC_S = idesc_f16(128, kTile, 1, 1, 0, 0);
             constexpr uint32_t IDESC_O = idesc_f16(128, D, 1, 1, 0, 1);
             const uint64_t dQ = smem_desc(smem_u32(sQ), 16, C::SBO, C::LAYOUT);
@@ -225,13 +229,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 const int e = kk * 16;
                 return (uint64_t)(((e / C::BOXC) * C::BOX_BYTES + (e % C::BOXC) * 2) >> 4);
             };
-            auto wait_ring = [&](int e) -> bool {
-                return mbar_wait(&ring_full[e % C::RING], (e / C::RING) & 1, p.err, &abort_sh);
+            auto probe = [](uint64_t *bar, uint32_t parity) -> bool {
+                return mbar_test_wait(smem_u32(bar), parity);
             };
+            bool ok = true;
+            auto need = [&](bool probed, uint64_t *bar, uint32_t parity) -> bool {
+                if (probed) return true;
+                if (!mbar_wait(bar, parity, p.err, &abort_sh)) ok = false;
+                return ok;
+            };
+            auto ring_bar = [&](int e) { return &ring_full[e % C::RING]; };
+            auto ring_par = [](int e) -> uint32_t { return (e / C::RING) & 1; };
             // Next item: its tile count, or 0 at the end of the list (or on failure).
-            auto next_item = [&](int k, bool &ok) -> int {
-                if (!mbar_wait(&item_full[k % kItemSlots], (k / kItemSlots) & 1, p.err,
-                               &abort_sh)) {
+            auto next_item = [&](int k) -> int {
+                if (!mbar_wait(&item_full[k % kItemSlots], (k / kItemSlots) & 1, p.err, &abort_sh)) {
                     ok = false;
                     return 0;
                 }
@@ -248,12 +259,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     umma_f16(d, dQb + kk_off(kk), dK + kk_off(kk), IDESC_S, kk != 0);
                 umma_commit(&s_full[b]);
             };
-            bool ok = true;
+            // O_b (+)= P_b(g) V(g); P_b sits in the first half of S_b's columns.
+            auto issue_pv = [&](int b, int g, bool first) {
+                const uint64_t dV =
+                    dRingV + (uint64_t)((((2 * g + 1) % C::RING) * C::TILE_BYTES) >> 4);
+                const uint32_t tP = tmem_base + b * kTile;
+                const uint32_t dO = tmem_base + 256 + b * 128;
+#pragma unroll
+                for (int kk = 0; kk < kTile / 16; ++kk)
+                    umma_f16_ts(dO, tP + kk * 8, dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O,
+                                !first || kk != 0);
+            };
             int k = 0, g = 0;  // local item, global tile counter
-            int n = next_item(0, ok);
+            int n = next_item(0);
             // First item's S0(0), S1(0).
             if (n > 0) {
-                if (!mbar_wait(&q_full[0], 0, p.err, &abort_sh) || !wait_ring(0)) {
+                if (!mbar_wait(&q_full[0], 0, p.err, &abort_sh) || !mbar_wait(ring_bar(0), 0, p.err, &abort_sh)) {
                     ok = false;
                     n = 0;
                 } else {
@@ -264,67 +285,57 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     if (n == 1) umma_commit(&q_empty[0]);
                 }
             }
+            bool pv_ok = false, s0_ok = false;  // probes: V(g) loaded, P_0(g) written
             while (ok && n > 0) {
-                int n_next = -1;  // tile count of item k + 1 once fetched
-                for (int j = 0; ok && j < n; ++j, ++g) {
-                    if (!wait_ring(2 * g + 1)) {
-                        ok = false;
+                int n_next = 0;
+                for (int j = 0; j < n; ++j, ++g) {
+                    // ---- PV_0(g)
+                    if (!need(pv_ok, ring_bar(2 * g + 1), ring_par(2 * g + 1)) ||
+                        !need(s0_ok, &s_free[0], g & 1) ||
+                        (j == 0 && !need(false, &o_free[0], (k & 1) ^ 1)))
                         break;
-                    }
-                    const uint64_t dV =
-                        dRingV + (uint64_t)((((2 * g + 1) % C::RING) * C::TILE_BYTES) >> 4);
-                    for (int b = 0; b < 2; ++b) {
-                        // PV_b(g): P_b(g) written, O_b free at an item's first tile.
-                        if (!mbar_wait(&s_free[b], g & 1, p.err, &abort_sh) ||
-                            (j == 0 &&
-                             !mbar_wait(&o_free[b], (k & 1) ^ 1, p.err, &abort_sh))) {
-                            ok = false;
-                            break;
-                        }
+                    tc_fence_after();
+                    const bool last = j + 1 == n;
+                    bool k_ok = last ? false : probe(ring_bar(2 * g + 2), ring_par(2 * g + 2));
+                    issue_pv(0, g, j == 0);
+                    if (last) umma_commit(&o_full[0]);
+                    // ---- S_0(g + 1): next tile of this item, or tile 0 of the next item
+                    bool s1_ok;
+                    if (!last) {
+                        if (!need(k_ok, ring_bar(2 * g + 2), ring_par(2 * g + 2))) break;
                         tc_fence_after();
-                        const uint32_t tP = tmem_base + b * kTile;
-                        const uint32_t dO = tmem_base + 256 + b * 128;
-#pragma unroll
-                        for (int kk = 0; kk < kTile / 16; ++kk)
-                            umma_f16_ts(dO, tP + kk * 8,
-                                        dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O,
-                                        (j | kk) != 0);
-                        umma_commit(&pv_done[b]);
-                        if (j == n - 1) umma_commit(&o_full[b]);
-                        if (b == 1) umma_commit(&ring_empty[(2 * g + 1) % C::RING]);
-                        // Next S of block b: tile j + 1 of this item, or tile 0 of the next.
-                        if (j + 1 < n) {
-                            if (b == 0 && !wait_ring(2 * g + 2)) {
-                                ok = false;
+                        s1_ok = probe(&s_free[1], g & 1);
+                        issue_s(0, k, g + 1);
+                    } else {
+                        n_next = next_item(k + 1);
+                        if (!ok) break;
+                        if (n_next > 0) {
+                            if (!need(false, &q_full[(k + 1) & 1], ((k + 1) >> 1) & 1) ||
+                                !need(false, ring_bar(2 * g + 2), ring_par(2 * g + 2)))
                                 break;
-                            }
                             tc_fence_after();
-                            issue_s(b, k, g + 1);
-                            if (b == 1) {
-                                umma_commit(&ring_empty[(2 * g + 2) % C::RING]);
-                                if (j + 2 == n) umma_commit(&q_empty[k & 1]);
-                            }
-                        } else {
-                            if (b == 0) {
-                                n_next = next_item(k + 1, ok);
-                                if (n_next > 0 &&
-                                    (!mbar_wait(&q_full[(k + 1) & 1], ((k + 1) >> 1) & 1, p.err,
-                                                &abort_sh) ||
-                                     !wait_ring(2 * g + 2))) {
-                                    ok = false;
-                                    n_next = 0;
-                                }
-                                if (!ok) break;
-                            }
-                            if (n_next > 0) {
-                                tc_fence_after();
-                                issue_s(b, k + 1, g + 1);
-                                if (b == 1) {
-                                    umma_commit(&ring_empty[(2 * g + 2) % C::RING]);
-                                    if (n_next == 1) umma_commit(&q_empty[(k + 1) & 1]);
-                                }
-                            }
                         }
+                        s1_ok = probe(&s_free[1], g & 1);
+                        if (n_next > 0) issue_s(0, k + 1, g + 1);
+                    }
+                    // ---- PV_1(g)
+                    if (!need(s1_ok, &s_free[1], g & 1) ||
+                        (j == 0 && !need(false, &o_free[1], (k & 1) ^ 1)))
+                        break;
+                    tc_fence_after();
+                    issue_pv(1, g, j == 0);
+                    if (last) umma_commit(&o_full[1]);
+                    umma_commit(&ring_empty[(2 * g + 1) % C::RING]);
+                    // ---- S_1(g + 1)
+                    const bool more = !last || n_next > 0;
+                    if (more) {
+                        pv_ok = probe(ring_bar(2 * g + 3), ring_par(2 * g + 3));
+                        s0_ok = probe(&s_free[0], (g + 1) & 1);
+                        issue_s(1, last ? k + 1 : k, g + 1);
+                        umma_commit(&ring_empty[(2 * g + 2) % C::RING]);
+                        const int n_cur = last ? n_next : n;
+                        const int j_next = last ? 0 : j + 1;
+                        if (j_next + 1 == n_cur) umma_commit(&q_empty[(last ? k + 1 : k) & 1]);
                     }
                 }
                 if (!ok) break;
@@ -346,16 +357,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
         const uint32_t tS = tmem_base + lane_off + b * kTile;
         const uint32_t tO = tmem_base + lane_off + 256 + b * 128;
+        // An item's O is written out after the next item's first P: the wait for
+        // the item's last PV then overlaps that tile's softmax (PV_b of the
+        // next item waits for both arrivals, so O_b still holds the item here).
+        bool pend = false, p_store = false;
+        __nv_bfloat16 *p_orow = nullptr;
+        float p_l = 0.0f;
+        int p_k = 0;
+        auto flush = [&]() -> bool {
+            pend = false;
+            if (!mbar_wait(&o_full[b], p_k & 1, p.err, &abort_sh)) return false;
+            tc_fence_after();
+            const float inv = p_l > 0.0f ? 1.0f / p_l : 0.0f;
+#pragma unroll 1
+            for (int c = 0; c < D / C::CW; ++c) {
+                float o[C::CW];
+                if constexpr (C::CW == 32)
+                    tmem_ld32(tO + c * 32, o);
+                else
+                    tmem_ld16(tO + c * 16, o);
+                tmem_wait_ld();
+                if (p_store) {
+                    uint4 *op = reinterpret_cast<uint4 *>(p_orow + c * C::CW);
+#pragma unroll
+                    for (int u = 0; u < C::CW / 8; ++u)
+                        op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
+                                           pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
+                                           pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
+                                           pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free[b]);
+            return true;
+        };
         int g = 0;
-        for (int k = 0;; ++k) {
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
             if (!mbar_wait(&item_full[k % kItemSlots], (k / kItemSlots) & 1, p.err, &abort_sh))
                 break;
             const int idx = item_sh[k % kItemSlots];
             if (idx < 0) break;
             const ItemGeo it = item_geo(p, idx);
-            const int q = it.qt[b] * kTile + r;
+            const int q = (b ? it.qt1 : it.qt0) * kTile + r;
             float m_used = -INFINITY, l = 0.0f;
-            bool ok = true;
             for (int j = 0; j < it.n_kt; ++j, ++g) {
                 if (!mbar_wait(&s_full[b], g & 1, p.err, &abort_sh)) {
                     ok = false;
@@ -385,30 +431,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 mx[2] = max3(mx[2], mx[3], s[kTile - 3]);
                 const float rmax = max3(mx[0], mx[2], fmaxf(s[kTile - 2], s[kTile - 1]));
                 const float m_new = fmaxf(m_used, rmax * sl2);
-                if (j == 0) {
-                    m_used = m_new;
-                } else if (__any_sync(0xffffffffu, m_new > m_used + kRescaleLog2)) {
-                    // O may change only once PV_b(g - 1) has completed; PV_b(g)
-                    // waits for this tile's P.
-                    if (!mbar_wait(&pv_done[b], (g - 1) & 1, p.err, &abort_sh)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const float alpha = ex2_approx(m_used - m_new);
-#pragma unroll 1
-                    for (int c = 0; c < D / C::CW; ++c) {
-                        float o[32];
-                        tmem_ld32(tO + c * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(tO + c * 32, o);
-                    }
-                    tmem_wait_st();
-                    l *= alpha;
-                    m_used = m_new;
-                }
+                const bool rescale = j > 0 && __any_sync(0xffffffffu, m_new > m_used + kRescaleLog2);
+                const float m_old = m_used;
+                if (j == 0 || rescale) m_used = m_new;
                 // P over the first 64 columns of the score buffer: key 2c, 2c + 1 in
                 // column c.  Every eighth pair goes through the FMA-pipe exp2.
                 float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -434,40 +459,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     tmem_st32u(tS + h * 32, pk);
                 }
                 tmem_wait_st();
+                if (rescale) {
+                    // PV_b(g - 1) has completed: S_b(g), whose completion this
+                    // thread waited for, was issued after it.  PV_b(g) waits for
+                    // the s_free arrival below.
+                    const float alpha = ex2_approx(m_old - m_used);
+#pragma unroll 1
+                    for (int c = 0; c < D / C::CW; ++c) {
+                        float o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(tO + c * 32, o);
+                    }
+                    tmem_wait_st();
+                    l *= alpha;
+                }
                 l += (la[0] + la[1]) + (la[2] + la[3]);
+                if (j == 0 && pend && !flush()) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_free[b]);
             }
             if (!ok) break;
-            // Item done: write O / l, release O_b.
-            if (!mbar_wait(&o_full[b], k & 1, p.err, &abort_sh)) break;
-            tc_fence_after();
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            const bool store = q < it.L && (b == 0 || it.store1);
-            __nv_bfloat16 *orow = p.out + (size_t)(it.seq0 + q) * p.ldo + it.h[b] * D;
-#pragma unroll 1
-            for (int c = 0; c < D / C::CW; ++c) {
-                float o[C::CW];
-                if constexpr (C::CW == 32)
-                    tmem_ld32(tO + c * 32, o);
-                else
-                    tmem_ld16(tO + c * 16, o);
-                tmem_wait_ld();
-                if (store) {
-                    uint4 *op = reinterpret_cast<uint4 *>(orow + c * C::CW);
-#pragma unroll
-                    for (int u = 0; u < C::CW / 8; ++u)
-                        op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
-                                           pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
-                                           pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
-                                           pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&o_free[b]);
+            pend = true;
+            p_store = q < it.L && (b == 0 || it.store1);
+            p_orow = p.out + (size_t)(it.seq0 + q) * p.ldo + (b ? it.h1 : it.h0) * D;
+            p_l = l;
+            p_k = k;
         }
+        if (ok && pend) flush();
     }
 
     tc_fence_before();
