@@ -195,6 +195,7 @@ struct Device {
     float *pos_table = nullptr, *type0 = nullptr, *emb_ln_g = nullptr, *emb_ln_b = nullptr;
     float *final_norm = nullptr;
     float *rope_cos = nullptr, *rope_sin = nullptr;
+    __half *rope_cos_h = nullptr, *rope_sin_h = nullptr;  // f16 copies for the bf16 GEMM
     int rope_cap = 0;
     std::vector<LayerW> layers;
     Workspace ws;
@@ -346,12 +347,23 @@ int ensure_rope(Device &D, const ffwd_config_t &c, int n_pos) {
     }
     CK(cudaSetDevice(D.dev));
     CK(cudaStreamSynchronize(D.stream));
+    std::vector<__half> hch(hc.size()), hsh(hs.size());
+    for (size_t i = 0; i < hc.size(); ++i) {
+        hch[i] = __float2half_rn(hc[i]);
+        hsh[i] = __float2half_rn(hs[i]);
+    }
     if (D.rope_cos) CK(cudaFree(D.rope_cos));
     if (D.rope_sin) CK(cudaFree(D.rope_sin));
+    if (D.rope_cos_h) CK(cudaFree(D.rope_cos_h));
+    if (D.rope_sin_h) CK(cudaFree(D.rope_sin_h));
     CK(cudaMalloc(&D.rope_cos, hc.size() * 4));
     CK(cudaMalloc(&D.rope_sin, hs.size() * 4));
+    CK(cudaMalloc(&D.rope_cos_h, hch.size() * 2));
+    CK(cudaMalloc(&D.rope_sin_h, hsh.size() * 2));
     CK(cudaMemcpy(D.rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(D.rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(D.rope_cos_h, hch.data(), hch.size() * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(D.rope_sin_h, hsh.data(), hsh.size() * 2, cudaMemcpyHostToDevice));
     D.rope_cap = cap;
     return 0;
 }
@@ -498,7 +510,7 @@ void free_device(Device &D) {
     Workspace &w = D.ws;
     void *dptrs[] = {w.ids, w.pos, w.offsets, w.err, w.span_starts, w.span_ends, w.items, w.pooled,
                      w.x, w.xb, w.xb_lo, w.qkv, w.att, w.att_lo, w.hmid, w.hmid_lo, D.rope_cos,
-                     D.rope_sin};
+                     D.rope_sin, D.rope_cos_h, D.rope_sin_h};
     for (void *q : dptrs)
         if (q) cudaFree(q);
     void *hptrs[] = {w.h_ids, w.h_offsets, w.h_err, w.h_items, w.h_out, w.h_spans};
@@ -738,6 +750,8 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
             p.pos = w.pos;
             p.rope_cos = D.rope_cos;
             p.rope_sin = D.rope_sin;
+            p.rope_cos_h = D.rope_cos_h;
+            p.rope_sin_h = D.rope_sin_h;
             p.q_norm = l.q_norm;
             p.k_norm = l.k_norm;
             p.n_q_heads = c.n_heads;

@@ -11,6 +11,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 namespace fb {
 
@@ -45,6 +46,8 @@ struct GemmParams {
     const int *pos;        // [M] position of each packed row
     const float *rope_cos; // [n_pos, head_dim / 2]
     const float *rope_sin;
+    const __half *rope_cos_h;  // the same tables in f16 (single-pass bf16 GEMM)
+    const __half *rope_sin_h;
     const float *q_norm;   // [head_dim] or null (no QK-norm)
     const float *k_norm;
     int n_q_heads, n_kv_heads, head_dim;

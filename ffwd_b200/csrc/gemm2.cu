@@ -98,6 +98,7 @@ __device__ __forceinline__ void arrive_leader(uint64_t *bar) {
 // chunks per warpgroup alternate; rows past M are clipped by the tensor map.
 struct TmaSink {
     static constexpr bool kAllRows = true;  // every row takes part in the barriers
+    static constexpr bool kHalfRope = true;  // single-pass bf16 only: RoPE from f16 tables
     const GemmParams &p;
     const CUtensorMap *map;
     uint8_t *stage;  // this warpgroup's two chunks

@@ -69,6 +69,7 @@ __device__ __forceinline__ void store_row32(const GemmParams &p, int row, int co
 // Writes each thread's row segments straight to global memory.
 struct DirectSink {
     static constexpr bool kAllRows = false;  // rows past M skip their work
+    static constexpr bool kHalfRope = false;  // RoPE from the f32 tables
     const GemmParams &p;
     int grow;
     __device__ __forceinline__ void put(const float (&v)[32], int col) { store_row32(p, grow, col, v); }
@@ -172,6 +173,69 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                     for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
                 }
                 inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
+            }
+            if constexpr (Sink::kHalfRope) {
+                // f16 tables: each chunk's cos / sin (64 halves) are loaded before
+                // its TMEM reads (the first) or between the previous chunk's two
+                // stores, so the L2 latency overlaps other work.
+                const uint4 *c8 = reinterpret_cast<const uint4 *>(p.rope_cos_h + (size_t)ps * half);
+                const uint4 *s8 = reinterpret_cast<const uint4 *>(p.rope_sin_h + (size_t)ps * half);
+                uint4 cv[4], sv[4];
+                if (half >= 32) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        cv[i] = __ldg(c8 + i);
+                        sv[i] = __ldg(s8 + i);
+                    }
+                }
+#pragma unroll 1
+                for (int c = 0; c < half / 32; ++c) {
+                    float x1[32], x2[32];
+                    tmem_ld32(tbase + h0 + c * 32, x1);
+                    tmem_ld32(tbase + h0 + half + c * 32, x2);
+                    tmem_wait_ld();
+                    if (p.bias) {
+                        add_bias32(x1, p.bias, col0 + c * 32);
+                        add_bias32(x2, p.bias, col0 + half + c * 32);
+                    }
+                    if (nw) {
+                        const float4 *w1 = reinterpret_cast<const float4 *>(nw + c * 32);
+                        const float4 *w2 = reinterpret_cast<const float4 *>(nw + half + c * 32);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 a = __ldg(w1 + i), b = __ldg(w2 + i);
+                            x1[4 * i] *= inv * a.x; x1[4 * i + 1] *= inv * a.y;
+                            x1[4 * i + 2] *= inv * a.z; x1[4 * i + 3] *= inv * a.w;
+                            x2[4 * i] *= inv * b.x; x2[4 * i + 1] *= inv * b.y;
+                            x2[4 * i + 2] *= inv * b.z; x2[4 * i + 3] *= inv * b.w;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __half2 *ch = reinterpret_cast<const __half2 *>(&cv[i]);
+                        const __half2 *sh = reinterpret_cast<const __half2 *>(&sv[i]);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const float2 cf = __half22float2(ch[u]), sf = __half22float2(sh[u]);
+                            const int e = 8 * i + 2 * u;
+                            const float a0 = x1[e], b0 = x2[e], a1 = x1[e + 1], b1 = x2[e + 1];
+                            x1[e] = a0 * cf.x - b0 * sf.x;
+                            x2[e] = b0 * cf.x + a0 * sf.x;
+                            x1[e + 1] = a1 * cf.y - b1 * sf.y;
+                            x2[e + 1] = b1 * cf.y + a1 * sf.y;
+                        }
+                    }
+                    sink.put(x1, col0 + c * 32);
+                    if (c + 1 < half / 32) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            cv[i] = __ldg(c8 + (c + 1) * 4 + i);
+                            sv[i] = __ldg(s8 + (c + 1) * 4 + i);
+                        }
+                    }
+                    sink.put(x2, col0 + half + c * 32);
+                }
+                continue;
             }
             const float *cs = p.rope_cos + (size_t)ps * half;
             const float *sn = p.rope_sin + (size_t)ps * half;
