@@ -63,21 +63,6 @@ struct AttnCfg {
     static_assert(RING >= 3, "K/V ring too small");
 };
 
-// exp2 on the FMA pipe for a share of the softmax elements, so that the
-// MUFU unit is not the bound: x = n + f with n = round(x), f in [-1/2, 1/2];
-// 2^f by a degree-3 polynomial (coefficients fitted to 2^f on [-1/2, 1/2] by
-// iteratively reweighted least squares in relative error: max relative error
-// 7.5e-5, far below the bf16 rounding of P), 2^n added to the exponent field.
-// x is clamped at -126 (-inf -> about 1e-38, which vanishes in the row sum).
-__device__ __forceinline__ float exp2_fma(float x) {
-    x = fmaxf(x, -126.0f);
-    const float t = x + 12582912.0f;  // 1.5 * 2^23: round(x) lands in the low mantissa bits
-    const float f = x - (t - 12582912.0f);
-    const float p = fmaf(fmaf(fmaf(0.0551716685f, f, 0.242611125f), f, 0.693260968f), f,
-                         0.999928057f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float r;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -435,26 +420,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 const float m_old = m_used;
                 if (j == 0 || rescale) m_used = m_new;
                 // P over the first 64 columns of the score buffer: key 2c, 2c + 1 in
-                // column c.  Every eighth pair goes through the FMA-pipe exp2.
-                float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                // column c.  (Moving a share of the exponentials to an FMA-pipe
+                // polynomial was measured slower: the softmax warps are bound by
+                // instruction issue, not by the MUFU unit.)
+                // Key pairs are scaled with one packed f32x2 FMA: the softmax warps
+                // are bound by instruction issue.  (A packed add for the row sum
+                // was measured to cost registers: it spills.)
+                float2 la[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+                const float2 scale2 = make_float2(sl2, sl2), neg_m2 = make_float2(-m_used, -m_used);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     uint32_t pk[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const int e0 = h * 64 + 2 * i;
-                        const float x0 = fmaf(s[e0], sl2, -m_used);
-                        const float x1 = fmaf(s[e0 + 1], sl2, -m_used);
-                        float p0, p1;
-                        if ((i & 3) == 3) {
-                            p0 = exp2_fma(x0);
-                            p1 = exp2_fma(x1);
-                        } else {
-                            p0 = ex2_approx(x0);
-                            p1 = ex2_approx(x1);
-                        }
-                        la[i & 3] += p0 + p1;
-                        pk[i] = pack_bf16x2(p0, p1);
+                        const float2 x = fma_f32x2(make_float2(s[e0], s[e0 + 1]), scale2, neg_m2);
+                        const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                        la[i & 1].x += pp.x; la[i & 1].y += pp.y;
+                        pk[i] = pack_bf16x2(pp.x, pp.y);
                     }
                     tmem_st32u(tS + h * 32, pk);
                 }
@@ -476,7 +459,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     tmem_wait_st();
                     l *= alpha;
                 }
-                l += (la[0] + la[1]) + (la[2] + la[3]);
+                l += (la[0].x + la[1].x) + (la[0].y + la[1].y);
                 if (j == 0 && pend && !flush()) {
                     ok = false;
                     break;

@@ -39,7 +39,7 @@ int g_gemm_mode = 0;         // 0 f32, 1 tf32, 2 bf16, 3 16f (reference default:
 int g_weight_override = -1;  // -1 file dtype, 0 f32, 1 bf16, 2 f16
 std::vector<int> g_devices;
 bool g_devices_set = false;
-int g_max_tokens = 65536;
+int g_max_tokens = 262144;
 thread_local std::string t_err;
 
 void fail(const char *fmt, ...) {
@@ -852,11 +852,19 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
     const ffwd_config_t &c = ctx->cfg;
     const int H = c.hidden_size;
     CK(cudaSetDevice(D.dev));
+    // Forwards of at most g_max_tokens rows, sized evenly: with n forwards
+    // needed, each aims at total / n tokens, so no small tail forward runs
+    // the whole layer stack for a few sequences.
+    long long total = 0;
+    for (int i : idx) total += inputs[i].n_tokens;
+    const long long n_fwd = (total + g_max_tokens - 1) / g_max_tokens;
+    const long long aim = n_fwd > 1 ? (total + n_fwd - 1) / n_fwd : total;
     size_t i0 = 0;
     while (i0 < idx.size()) {
         size_t i1 = i0;
         long long tok = 0;
-        while (i1 < idx.size() && (i1 == i0 || tok + inputs[idx[i1]].n_tokens <= g_max_tokens)) {
+        while (i1 < idx.size() &&
+               (i1 == i0 || (tok + inputs[idx[i1]].n_tokens <= g_max_tokens && tok < aim))) {
             tok += inputs[idx[i1]].n_tokens;
             ++i1;
         }

@@ -149,7 +149,8 @@ FFWD_B200_API int ffwd_b200_encode_spans_batch(ffwd_b200_ctx_t *ctx,
 FFWD_B200_API int ffwd_b200_set_devices(const int *devices, int n_devices);
 
 /* Largest packed token count one device forward holds; longer batches run as
- * several forwards (sequences are never split).  Default 65536. */
+ * several forwards of about equal size (sequences are never split).  Default
+ * 262144 (about 6 GB of activations for a 1024-wide model). */
 FFWD_B200_API int ffwd_b200_set_max_tokens(int max_tokens);
 
 /* Device-resident entry (single device, index dev of the context's set): ids

@@ -156,7 +156,7 @@ def test_max_tokens_chunking_matches(model_root):
     try:
         chunked = native.B200Model(d, gemm_mode="bf16").encode_batch(seqs)
     finally:
-        native.lib().ffwd_b200_set_max_tokens(65536)
+        native.lib().ffwd_b200_set_max_tokens(262144)
     assert np.array_equal(whole, chunked)
 
 
