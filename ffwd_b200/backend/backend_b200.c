@@ -6,8 +6,9 @@
  * encode forwarding (backend_cuda.c:124-130) and constants
  * (ffwd_scratch_nbytes 0, ffwd_default_batch_wait_us 1000).
  *
- * Late-interaction models (is_late, ffwd_rerank) are not served by this
- * backend: ffwd_activate fails for them with a reason. */
+ * Late-interaction models (is_late) load through ffwd_b200_late_load and serve
+ * ffwd_token_dim / ffwd_rerank like backend_cuda.c:99-156, with MaxSim scored
+ * on the device (ffwd_b200_late_rerank) instead of on the host. */
 #include "ffwd_b200_api.h"
 
 #include <math.h>
@@ -19,6 +20,7 @@ struct embed {
     int is_late;
     char *dir;
     ffwd_b200_ctx_t *ctx;
+    ffwd_b200_late_ctx_t *late_ctx;
 };
 
 FFWD_B200_API int ffwd_verbose = 0;
@@ -64,8 +66,12 @@ FFWD_B200_API ffwd_t *ffwd_open(const char *model_dir, int is_late, const ffwd_o
 
 FFWD_B200_API int ffwd_activate(ffwd_t *b, char *err, size_t errlen) {
     if (b->is_late) {
-        snprintf(err, errlen, "late-interaction models are not supported by the B200 backend");
-        return -1;
+        b->late_ctx = ffwd_b200_late_load(b->dir);
+        if (!b->late_ctx) {
+            snprintf(err, errlen, "failed to load late-interaction model");
+            return -1;
+        }
+        return 0;
     }
     b->ctx = ffwd_b200_load(b->dir);
     if (!b->ctx) {
@@ -82,6 +88,10 @@ FFWD_B200_API void ffwd_worker_free(ffwd_t *b) {
         ffwd_b200_free(b->ctx);
         b->ctx = NULL;
     }
+    if (b->late_ctx) {
+        ffwd_b200_late_free(b->late_ctx);
+        b->late_ctx = NULL;
+    }
 }
 
 FFWD_B200_API void ffwd_free(ffwd_t *b) {
@@ -93,12 +103,13 @@ FFWD_B200_API void ffwd_free(ffwd_t *b) {
 }
 
 FFWD_B200_API const ffwd_config_t *ffwd_config(const ffwd_t *b) {
-    return b ? ffwd_b200_config(b->ctx) : NULL;
+    if (!b)
+        return NULL;
+    return b->is_late ? ffwd_b200_late_config(b->late_ctx) : ffwd_b200_config(b->ctx);
 }
 
 FFWD_B200_API int ffwd_token_dim(const ffwd_t *b) {
-    (void)b;
-    return 0;
+    return b && b->is_late ? ffwd_b200_late_token_dim(b->late_ctx) : 0;
 }
 
 FFWD_B200_API int ffwd_uses_dense_batches(const ffwd_t *b) {
@@ -116,10 +127,7 @@ FFWD_B200_API int ffwd_encode_spans_batch(ffwd_t *b, const ffwd_context_input_t 
 }
 
 FFWD_B200_API int ffwd_rerank(ffwd_t *b, const ffwd_rerank_input_t *in, float *scores) {
-    (void)b;
-    (void)in;
-    (void)scores;
-    return -1;
+    return b && b->late_ctx ? ffwd_b200_late_rerank(b->late_ctx, in, scores) : -1;
 }
 
 FFWD_B200_API size_t ffwd_scratch_nbytes(const ffwd_t *b) {

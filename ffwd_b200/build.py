@@ -27,7 +27,7 @@ NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
                   "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
-CU_SRCS = ["gemm.cu", "gemm2.cu", "attention.cu", "rowops.cu", "engine.cu"]
+CU_SRCS = ["gemm.cu", "gemm2.cu", "attention.cu", "rowops.cu", "late.cu", "engine.cu"]
 CC_SRCS = ["loader.cc"]
 
 LIB = os.path.join(LIBDIR, "libffwd_b200.so")

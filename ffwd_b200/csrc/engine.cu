@@ -13,6 +13,8 @@
 #include "gemm.cuh"
 #include "loader.h"
 #include "ptx.cuh"
+#include "late.cuh"
+#include <sys/stat.h>
 #include "rowops.cuh"
 
 #include <algorithm>
@@ -202,6 +204,14 @@ struct Device {
     Workspace *active_ws = nullptr;  // when set, step() uses these buffers instead of ws
     FwdState fs;
     std::vector<void *> allocs;
+    // Late interaction (first device of a late-interaction context).
+    float *late_wt = nullptr;   // 1_Dense weight transposed: [hidden, token_dim] f32
+    float *late_vec = nullptr;  // token vectors [late_cap_rows, token_dim]
+    int *late_rows = nullptr, *late_doff = nullptr;
+    float *late_scores = nullptr;
+    int *h_late_rows = nullptr, *h_late_doff = nullptr;
+    float *h_late_vec = nullptr, *h_late_scores = nullptr;
+    size_t late_cap_rows = 0, late_cap_docs = 0;
 };
 
 }  // namespace
@@ -212,6 +222,13 @@ struct ffwd_b200_ctx {
     int prec = 0;  // 0 bf16, 2 split 2-pass, 3 split 3-pass
     std::vector<fb::Device> devs;
     float lin_flops_per_token = 0.0f;
+    int token_dim = 0;  // late interaction: 1_Dense output width (0: pooled model)
+};
+
+// A late-interaction model: the base model context plus its 1_Dense head (on
+// the base context's first device).
+struct ffwd_b200_late_ctx {
+    ffwd_b200_ctx *base = nullptr;
 };
 
 namespace fb {
@@ -515,6 +532,12 @@ void free_device(Device &D) {
         if (q) cudaFree(q);
     void *hptrs[] = {w.h_ids, w.h_offsets, w.h_err, w.h_items, w.h_out, w.h_spans};
     for (void *q : hptrs)
+        if (q) cudaFreeHost(q);
+    void *lptrs[] = {D.late_wt, D.late_vec, D.late_rows, D.late_doff, D.late_scores};
+    for (void *q : lptrs)
+        if (q) cudaFree(q);
+    void *lhptrs[] = {D.h_late_rows, D.h_late_doff, D.h_late_vec, D.h_late_scores};
+    for (void *q : lhptrs)
         if (q) cudaFreeHost(q);
     if (D.stream) cudaStreamDestroy(D.stream);
     D = Device();
@@ -939,6 +962,16 @@ int validate_inputs(const ffwd_b200_ctx *ctx, const ffwd_input_t *inputs, int ba
     return 0;
 }
 
+// True if model_dir carries a 1_Dense projection head (a late-interaction
+// model), libffwd/model.c:25-28.
+bool has_late_projection(const std::string &dir) {
+    struct stat st;
+    return stat((dir + "/1_Dense/config.json").c_str(), &st) == 0 &&
+           stat((dir + "/1_Dense/model.safetensors").c_str(), &st) == 0;
+}
+
+ffwd_b200_ctx *load_ctx(const char *model_dir);
+
 }  // namespace
 }  // namespace fb
 
@@ -988,6 +1021,23 @@ FFWD_B200_API long long ffwd_b200_launch_count(void) { return g_launches.load();
 FFWD_B200_API ffwd_b200_ctx_t *ffwd_b200_load(const char *model_dir) {
     t_err.clear();
     if (!model_dir) return nullptr;
+    // A 1_Dense head makes the directory a late-interaction model, which is not
+    // a pooled embedding model (libffwd/model.c:308-314).
+    if (has_late_projection(model_dir)) {
+        fail("load %s: late-interaction models require token-level MaxSim support and are not "
+             "valid pooled embedding models (use ffwd_b200_late_load)",
+             model_dir);
+        return nullptr;
+    }
+    return load_ctx(model_dir);
+}
+
+}  // extern "C"
+
+namespace fb {
+namespace {
+
+ffwd_b200_ctx *load_ctx(const char *model_dir) {
     auto hm = std::make_unique<HostModel>();
     std::string err;
     if (!parse_model_config(model_dir, hm->cfg, err) || !hm->st.open(model_dir, err)) {
@@ -1081,6 +1131,11 @@ FFWD_B200_API ffwd_b200_ctx_t *ffwd_b200_load(const char *model_dir) {
     }
     return ctx;
 }
+
+}  // namespace
+}  // namespace fb
+
+extern "C" {
 
 FFWD_B200_API void ffwd_b200_free(ffwd_b200_ctx_t *ctx) {
     if (!ctx) return;
@@ -1338,6 +1393,291 @@ FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const voi
                            sms, 0));
     }
     CK(cudaDeviceSynchronize());
+    return 0;
+}
+
+}  // extern "C"
+
+// ====================================================================== late interaction
+//
+// Mirrors libffwd/cuda.h:35-60 (ffwd_cuda_late_*) on top of the pooled
+// engine: one packed forward, then the kept rows' token vectors (final norm,
+// 1_Dense projection, L2) on the device.  ffwd_b200_late_rerank also scores
+// MaxSim on the device; the reference scores on the host after copying every
+// token vector back (backend_cuda.c:132-156).
+namespace fb {
+namespace {
+
+int ensure_late(Device &D, size_t rows, size_t docs, int dim) {
+    if (rows > D.late_cap_rows) {
+        CK(cudaStreamSynchronize(D.stream));
+        if (D.late_vec) CK(cudaFree(D.late_vec));
+        if (D.late_rows) CK(cudaFree(D.late_rows));
+        if (D.h_late_rows) CK(cudaFreeHost(D.h_late_rows));
+        if (D.h_late_vec) CK(cudaFreeHost(D.h_late_vec));
+        D.late_vec = nullptr;
+        D.late_rows = D.h_late_rows = nullptr;
+        D.h_late_vec = nullptr;
+        const size_t cap = std::max(rows, 2 * D.late_cap_rows);
+        D.late_cap_rows = 0;
+        CK(cudaMalloc(&D.late_vec, cap * dim * sizeof(float)));
+        CK(cudaMalloc(&D.late_rows, cap * sizeof(int)));
+        CK(cudaMallocHost(&D.h_late_rows, cap * sizeof(int)));
+        CK(cudaMallocHost(&D.h_late_vec, cap * dim * sizeof(float)));
+        D.late_cap_rows = cap;
+    }
+    if (docs > D.late_cap_docs) {
+        CK(cudaStreamSynchronize(D.stream));
+        if (D.late_doff) CK(cudaFree(D.late_doff));
+        if (D.late_scores) CK(cudaFree(D.late_scores));
+        if (D.h_late_doff) CK(cudaFreeHost(D.h_late_doff));
+        if (D.h_late_scores) CK(cudaFreeHost(D.h_late_scores));
+        D.late_doff = D.h_late_doff = nullptr;
+        D.late_scores = D.h_late_scores = nullptr;
+        const size_t cap = std::max(docs, 2 * D.late_cap_docs);
+        D.late_cap_docs = 0;
+        CK(cudaMalloc(&D.late_doff, (cap + 1) * sizeof(int)));
+        CK(cudaMalloc(&D.late_scores, cap * sizeof(float)));
+        CK(cudaMallocHost(&D.h_late_doff, (cap + 1) * sizeof(int)));
+        CK(cudaMallocHost(&D.h_late_scores, cap * sizeof(float)));
+        D.late_cap_docs = cap;
+    }
+    return 0;
+}
+
+// One packed forward of inputs[0..n) on the context's first device, then the
+// token vectors of the packed rows h_rows[0..n_rows) (filled by the caller
+// into D.h_late_rows) into D.late_vec.  The stream is left running.
+int late_forward(ffwd_b200_ctx *ctx, const ffwd_input_t *inputs, int n, int n_rows,
+                 int normalize) {
+    const ffwd_config_t &c = ctx->cfg;
+    Device &D = ctx->devs[0];
+    if (validate_inputs(ctx, inputs, n)) return -1;
+    long long T = 0;
+    for (int b = 0; b < n; ++b) T += inputs[b].n_tokens;
+    if (T > g_max_tokens) {
+        fail("late-interaction batch of %lld tokens exceeds the %d-token forward", T, g_max_tokens);
+        return -1;
+    }
+    if (ensure_ws(ctx, D, (int)T, n, 0, 0)) return -1;
+    Workspace &w = D.ws;
+    int off = 0;
+    for (int b = 0; b < n; ++b) {
+        for (int t = 0; t < inputs[b].n_tokens; ++t) {
+            const int id = inputs[b].ids[t];
+            if (id < 0 || id >= c.vocab_size) {
+                fail("invalid token id %d at input %d position %d", id, b, t);
+                return -1;
+            }
+        }
+        w.h_offsets[b] = off;
+        memcpy(w.h_ids + off, inputs[b].ids, (size_t)inputs[b].n_tokens * 4);
+        off += inputs[b].n_tokens;
+    }
+    w.h_offsets[n] = off;
+    CK(cudaMemcpyAsync(w.ids, w.h_ids, (size_t)T * 4, cudaMemcpyHostToDevice, D.stream));
+    CK(cudaMemcpyAsync(w.offsets, w.h_offsets, (size_t)(n + 1) * 4, cudaMemcpyHostToDevice,
+                       D.stream));
+    CK(cudaMemsetAsync(w.err, 0, 4, D.stream));
+    if (forward(ctx, D, (int)T, n, w.h_offsets)) return -1;
+    CK(cudaMemcpyAsync(D.late_rows, D.h_late_rows, (size_t)n_rows * 4, cudaMemcpyHostToDevice,
+                       D.stream));
+    LAUNCH(late_project_launch(w.x, c.hidden_size, D.late_rows, n_rows,
+                               c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm,
+                               c.rms_norm_eps, D.late_wt, ctx->token_dim, normalize, D.late_vec,
+                               w.err, D.stream));
+    return 0;
+}
+
+// Copy n_rows token vectors to out and check the device error word.
+int late_fetch(ffwd_b200_ctx *ctx, int n_rows, float *out) {
+    Device &D = ctx->devs[0];
+    const size_t bytes = (size_t)n_rows * ctx->token_dim * sizeof(float);
+    CK(cudaMemcpyAsync(D.h_late_vec, D.late_vec, bytes, cudaMemcpyDeviceToHost, D.stream));
+    CK(cudaMemcpyAsync(D.ws.h_err, D.ws.err, 4, cudaMemcpyDeviceToHost, D.stream));
+    CK(cudaStreamSynchronize(D.stream));
+    if (check_err(D)) return -1;
+    memcpy(out, D.h_late_vec, bytes);
+    return 0;
+}
+
+// Reference input checks of ffwd_late_model_encode_docs (late_blas.c:117-134).
+int late_check_docs(const int *const *doc_ids, const int *n_tokens, const int *const *keep,
+                    const int *n_keep, int n_docs, long long *total_keep) {
+    long long tk = 0;
+    for (int d = 0; d < n_docs; ++d) {
+        if (!doc_ids[d] || n_tokens[d] <= 0 || !keep[d] || n_keep[d] <= 0 ||
+            n_keep[d] > n_tokens[d] || tk > INT32_MAX - n_keep[d]) {
+            fail("document %d: empty, or kept count outside [1, n_tokens]", d);
+            return -1;
+        }
+        for (int k = 0; k < n_keep[d]; ++k)
+            if (keep[d][k] < 0 || keep[d][k] >= n_tokens[d]) {
+                fail("document %d: kept index %d outside [0, %d)", d, keep[d][k], n_tokens[d]);
+                return -1;
+            }
+        tk += n_keep[d];
+    }
+    *total_keep = tk;
+    return 0;
+}
+
+}  // namespace
+}  // namespace fb
+
+extern "C" {
+
+FFWD_B200_API ffwd_b200_late_ctx_t *ffwd_b200_late_load(const char *model_dir) {
+    t_err.clear();
+    if (!model_dir) return nullptr;
+    if (!has_late_projection(model_dir)) {
+        fail("late load %s: missing 1_Dense projection", model_dir);
+        return nullptr;
+    }
+    SafeTensors st;
+    std::string err;
+    const std::string dense = std::string(model_dir) + "/1_Dense";
+    if (!st.open(dense, err)) {
+        fail("late load %s: cannot open %s/model.safetensors: %s", model_dir, dense.c_str(),
+             err.c_str());
+        return nullptr;
+    }
+    const TensorView *t = st.find("linear.weight");
+    if (!t) {
+        fail("late load %s: missing linear.weight", model_dir);
+        return nullptr;
+    }
+    ffwd_b200_ctx *base = load_ctx(model_dir);
+    if (!base) return nullptr;
+    const int H = base->cfg.hidden_size;
+    std::vector<float> w;
+    if (t->shape.size() != 2 || t->shape[0] <= 0 || t->shape[0] > kLateMaxDim ||
+        !tensor_to_f32(t, {t->shape[0], (int64_t)H}, w, err, "linear.weight")) {
+        fail("late load %s: bad projection %s (token_dim must be in [1, %d], in = hidden %d)",
+             model_dir, err.c_str(), kLateMaxDim, H);
+        ffwd_b200_free(base);
+        return nullptr;
+    }
+    const int dim = (int)t->shape[0];
+    std::vector<float> wt((size_t)H * dim);
+    for (int o = 0; o < dim; ++o)
+        for (int h = 0; h < H; ++h) wt[(size_t)h * dim + o] = w[(size_t)o * H + h];
+    Device &D = base->devs[0];
+    if (cudaSetDevice(D.dev) != cudaSuccess || cudaMalloc(&D.late_wt, wt.size() * 4) != cudaSuccess ||
+        cudaMemcpy(D.late_wt, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        fail("late load %s: projection upload failed", model_dir);
+        ffwd_b200_free(base);
+        return nullptr;
+    }
+    base->token_dim = dim;
+    auto *ctx = new ffwd_b200_late_ctx();
+    ctx->base = base;
+    return ctx;
+}
+
+FFWD_B200_API void ffwd_b200_late_free(ffwd_b200_late_ctx_t *ctx) {
+    if (!ctx) return;
+    ffwd_b200_free(ctx->base);
+    delete ctx;
+}
+
+FFWD_B200_API const ffwd_config_t *ffwd_b200_late_config(const ffwd_b200_late_ctx_t *ctx) {
+    return ctx ? &ctx->base->cfg : nullptr;
+}
+
+FFWD_B200_API int ffwd_b200_late_token_dim(const ffwd_b200_late_ctx_t *ctx) {
+    return ctx ? ctx->base->token_dim : 0;
+}
+
+FFWD_B200_API int ffwd_b200_late_encode_tokens(ffwd_b200_late_ctx_t *ctx, const int *token_ids,
+                                               int n_tokens, int normalize, float *out_vectors) {
+    t_err.clear();
+    if (!ctx || !token_ids || n_tokens <= 0 || !out_vectors) {
+        fail("invalid arguments");
+        return -1;
+    }
+    ffwd_b200_ctx *b = ctx->base;
+    Device &D = b->devs[0];
+    CK(cudaSetDevice(D.dev));
+    if (ensure_late(D, (size_t)n_tokens, 0, b->token_dim)) return -1;
+    for (int i = 0; i < n_tokens; ++i) D.h_late_rows[i] = i;
+    const ffwd_input_t in = {token_ids, n_tokens};
+    if (late_forward(b, &in, 1, n_tokens, normalize)) return -1;
+    return late_fetch(b, n_tokens, out_vectors);
+}
+
+FFWD_B200_API int ffwd_b200_late_encode_docs(ffwd_b200_late_ctx_t *ctx, const int *const *doc_ids,
+                                             const int *n_tokens, const int *const *keep,
+                                             const int *n_keep, int n_docs, int normalize,
+                                             float *out_vectors, int *out_offsets) {
+    t_err.clear();
+    if (!ctx || !doc_ids || !n_tokens || !keep || !n_keep || n_docs <= 0 || !out_vectors ||
+        !out_offsets) {
+        fail("invalid arguments");
+        return -1;
+    }
+    long long total_keep = 0;
+    if (late_check_docs(doc_ids, n_tokens, keep, n_keep, n_docs, &total_keep)) return -1;
+    ffwd_b200_ctx *b = ctx->base;
+    Device &D = b->devs[0];
+    CK(cudaSetDevice(D.dev));
+    if (ensure_late(D, (size_t)total_keep, 0, b->token_dim)) return -1;
+    std::vector<ffwd_input_t> inputs(n_docs);
+    int pos = 0, start = 0;
+    out_offsets[0] = 0;
+    for (int d = 0; d < n_docs; ++d) {
+        inputs[d] = ffwd_input_t{doc_ids[d], n_tokens[d]};
+        for (int k = 0; k < n_keep[d]; ++k) D.h_late_rows[pos++] = start + keep[d][k];
+        start += n_tokens[d];
+        out_offsets[d + 1] = pos;
+    }
+    if (late_forward(b, inputs.data(), n_docs, (int)total_keep, normalize)) return -1;
+    return late_fetch(b, (int)total_keep, out_vectors);
+}
+
+FFWD_B200_API int ffwd_b200_late_rerank(ffwd_b200_late_ctx_t *ctx, const ffwd_rerank_input_t *in,
+                                        float *scores) {
+    t_err.clear();
+    if (!ctx || !in || !scores || !in->query_ids || in->query_n_tokens <= 0 ||
+        in->query_n_keep <= 0 || in->query_n_keep > in->query_n_tokens || in->n_docs <= 0 ||
+        !in->doc_ids || !in->doc_n_tokens || !in->doc_keep || !in->doc_n_keep) {
+        fail("invalid arguments");
+        return -1;
+    }
+    long long total_keep = 0;
+    if (late_check_docs(in->doc_ids, in->doc_n_tokens, in->doc_keep, in->doc_n_keep, in->n_docs,
+                        &total_keep))
+        return -1;
+    ffwd_b200_ctx *b = ctx->base;
+    Device &D = b->devs[0];
+    CK(cudaSetDevice(D.dev));
+    const int qk = in->query_n_keep, dim = b->token_dim;
+    if (ensure_late(D, (size_t)qk + total_keep, (size_t)in->n_docs, dim)) return -1;
+    // Query and candidates in one packed forward; the query's first
+    // query_n_keep vectors score against each candidate's kept vectors.
+    std::vector<ffwd_input_t> inputs(in->n_docs + 1);
+    inputs[0] = ffwd_input_t{in->query_ids, in->query_n_tokens};
+    int pos = 0;
+    for (int i = 0; i < qk; ++i) D.h_late_rows[pos++] = i;
+    int start = in->query_n_tokens;
+    D.h_late_doff[0] = 0;
+    for (int d = 0; d < in->n_docs; ++d) {
+        inputs[d + 1] = ffwd_input_t{in->doc_ids[d], in->doc_n_tokens[d]};
+        for (int k = 0; k < in->doc_n_keep[d]; ++k) D.h_late_rows[pos++] = start + in->doc_keep[d][k];
+        start += in->doc_n_tokens[d];
+        D.h_late_doff[d + 1] = pos - qk;
+    }
+    if (late_forward(b, inputs.data(), in->n_docs + 1, pos, 1)) return -1;
+    CK(cudaMemcpyAsync(D.late_doff, D.h_late_doff, (size_t)(in->n_docs + 1) * 4,
+                       cudaMemcpyHostToDevice, D.stream));
+    LAUNCH(late_maxsim_launch(D.late_vec, qk, D.late_vec + (size_t)qk * dim, D.late_doff,
+                              in->n_docs, dim, D.late_scores, D.stream));
+    CK(cudaMemcpyAsync(D.h_late_scores, D.late_scores, (size_t)in->n_docs * 4,
+                       cudaMemcpyDeviceToHost, D.stream));
+    CK(cudaMemcpyAsync(D.ws.h_err, D.ws.err, 4, cudaMemcpyDeviceToHost, D.stream));
+    CK(cudaStreamSynchronize(D.stream));
+    if (check_err(D)) return -1;
+    memcpy(scores, D.h_late_scores, (size_t)in->n_docs * 4);
     return 0;
 }
 

@@ -47,6 +47,15 @@ class ffwd_config_t(ctypes.Structure):
             "append_terminal_token")]
 
 
+class ffwd_rerank_input_t(ctypes.Structure):
+    _fields_ = [("query_ids", ctypes.POINTER(ctypes.c_int)), ("query_n_tokens", ctypes.c_int),
+                ("query_n_keep", ctypes.c_int),
+                ("doc_ids", ctypes.POINTER(ctypes.POINTER(ctypes.c_int))),
+                ("doc_n_tokens", ctypes.POINTER(ctypes.c_int)),
+                ("doc_keep", ctypes.POINTER(ctypes.POINTER(ctypes.c_int))),
+                ("doc_n_keep", ctypes.POINTER(ctypes.c_int)), ("n_docs", ctypes.c_int)]
+
+
 class ffwd_options_t(ctypes.Structure):
     _fields_ = [("n_threads", ctypes.c_int), ("gpu_quant_bits", ctypes.c_int),
                 ("gpu_quant_group_size", ctypes.c_int), ("gpu_gemm_mode", ctypes.c_char_p),
@@ -87,6 +96,15 @@ ABI = {
     "ffwd_b200_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                            ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "ffwd_b200_late_load": (ctypes.c_void_p, [ctypes.c_char_p]),
+    "ffwd_b200_late_free": (None, [ctypes.c_void_p]),
+    "ffwd_b200_late_config": (ctypes.POINTER(ffwd_config_t), [ctypes.c_void_p]),
+    "ffwd_b200_late_token_dim": (ctypes.c_int, [ctypes.c_void_p]),
+    "ffwd_b200_late_encode_tokens": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_void_p]),
+    "ffwd_b200_late_encode_docs": (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_void_p] * 4 + [
+        ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "ffwd_b200_late_rerank": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
 }
 
 # The reference-facing public API (include/ffwd_b200_api.h).
@@ -261,6 +279,78 @@ class B200Model:
             pass
 
 
+class _DocArrays:
+    """Pointer arrays (int *const *) over a list of int32 arrays, kept alive."""
+
+    def __init__(self, arrays):
+        self.arrs = [np.ascontiguousarray(np.asarray(a, dtype=np.int32)) for a in arrays]
+        self.ptrs = (ctypes.POINTER(ctypes.c_int) * len(self.arrs))(
+            *[a.ctypes.data_as(ctypes.POINTER(ctypes.c_int)) for a in self.arrs])
+        self.lens = np.ascontiguousarray(np.array([a.size for a in self.arrs], dtype=np.int32))
+
+
+def rerank_input(query, query_n_keep, docs, keeps):
+    """ffwd_rerank_input_t over numpy arrays; returns (struct, keep-alive)."""
+    q = np.ascontiguousarray(np.asarray(query, dtype=np.int32))
+    d, k = _DocArrays(docs), _DocArrays(keeps)
+    rin = ffwd_rerank_input_t(q.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), int(q.size),
+                              int(query_n_keep), d.ptrs,
+                              d.lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), k.ptrs,
+                              k.lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), len(d.arrs))
+    return rin, (q, d, k)
+
+
+class B200Late:
+    """A late-interaction model (the reference's ffwd_cuda_late_ctx_t)."""
+
+    def __init__(self, model_dir: str, gemm_mode: str | None = None):
+        L = lib()
+        if gemm_mode is not None and L.ffwd_b200_set_fast_gemm(gemm_mode.encode()) != 0:
+            raise FfwdError("--gpu-gemm-mode must be f32, tf32, bf16, or 16f")
+        self._l = L
+        self.h = L.ffwd_b200_late_load(model_dir.encode())
+        if not self.h:
+            raise FfwdError(f"failed to load late model: {last_error()}")
+        self.config = L.ffwd_b200_late_config(self.h).contents
+        self.dim = L.ffwd_b200_late_token_dim(self.h)
+
+    def encode_tokens(self, ids, normalize=True) -> np.ndarray:
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        out = np.zeros((a.size, self.dim), dtype=np.float32)
+        if self._l.ffwd_b200_late_encode_tokens(self.h, a.ctypes.data, int(a.size),
+                                                int(normalize), out.ctypes.data) != 0:
+            raise FfwdError(f"late_encode_tokens failed: {last_error()}")
+        return out
+
+    def encode_docs(self, docs, keeps, normalize=True):
+        d, k = _DocArrays(docs), _DocArrays(keeps)
+        out = np.zeros((int(k.lens.sum()), self.dim), dtype=np.float32)
+        offs = np.zeros(len(docs) + 1, dtype=np.int32)
+        if self._l.ffwd_b200_late_encode_docs(self.h, d.ptrs, d.lens.ctypes.data, k.ptrs,
+                                              k.lens.ctypes.data, len(docs), int(normalize),
+                                              out.ctypes.data, offs.ctypes.data) != 0:
+            raise FfwdError(f"late_encode_docs failed: {last_error()}")
+        return out, offs
+
+    def rerank(self, query, query_n_keep, docs, keeps) -> np.ndarray:
+        rin, keep = rerank_input(query, query_n_keep, docs, keeps)
+        scores = np.zeros(len(docs), dtype=np.float32)
+        if self._l.ffwd_b200_late_rerank(self.h, ctypes.byref(rin), scores.ctypes.data) != 0:
+            raise FfwdError(f"late_rerank failed: {last_error()}")
+        return scores
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._l.ffwd_b200_late_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def launch_count() -> int:
     return int(lib().ffwd_b200_launch_count())
 
@@ -283,7 +373,7 @@ class FfwdApi:
     """The reference's public API (libffwd/ffwd.h) served by libffwd_b200_api.so."""
 
     def __init__(self, model_dir: str, gemm_mode: str | None = None,
-                 weight_dtype: str | None = None):
+                 weight_dtype: str | None = None, is_late: bool = False):
         A = api()
         self._a = A
         err = ctypes.create_string_buffer(256)
@@ -291,7 +381,7 @@ class FfwdApi:
                               weight_dtype.encode() if weight_dtype else None, 0.0)
         if A.ffwd_init(ctypes.byref(opts), err, 256) != 0:
             raise FfwdError(err.value.decode())
-        self.e = A.ffwd_open(model_dir.encode(), 0, ctypes.byref(opts), err, 256)
+        self.e = A.ffwd_open(model_dir.encode(), int(is_late), ctypes.byref(opts), err, 256)
         if not self.e:
             raise FfwdError(err.value.decode())
         if A.ffwd_activate(self.e, err, 256) != 0:
@@ -300,6 +390,16 @@ class FfwdApi:
             raise FfwdError(err.value.decode())
         self.config = A.ffwd_config(self.e).contents
         self.hidden = self.config.hidden_size
+
+    def token_dim(self) -> int:
+        return self._a.ffwd_token_dim(self.e)
+
+    def rerank(self, query, query_n_keep, docs, keeps) -> np.ndarray:
+        rin, keep = rerank_input(query, query_n_keep, docs, keeps)
+        scores = np.zeros(len(docs), dtype=np.float32)
+        if self._a.ffwd_rerank(self.e, ctypes.byref(rin), scores.ctypes.data) != 0:
+            raise FfwdError("ffwd_rerank failed")
+        return scores
 
     def encode_batch_into(self, ins, n, out) -> int:
         return self._a.ffwd_encode_batch(self.e, ins, n, out)

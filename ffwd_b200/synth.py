@@ -58,6 +58,7 @@ class ModelSpec:
     hidden_act: str = "gelu"
     is_causal: bool | None = None
     seed: int = 0
+    late_dim: int = 0         # > 0: late-interaction model with a 1_Dense head [late_dim, hidden]
 
 
 # The five BASELINE configurations (shapes exactly as stated there).
@@ -287,11 +288,36 @@ def write_model(s: ModelSpec, out_dir: str, max_shard_bytes: int = 4 << 30) -> s
                     f.write(f32_to_bf16_bits(v).tobytes())
                 else:
                     f.write(v.astype(np.float32).tobytes())
+    if s.late_dim > 0:
+        write_late_projection(s, out_dir)
     return out_dir
 
 
+def write_late_projection(s: ModelSpec, out_dir: str) -> None:
+    """1_Dense head of a late-interaction model: ``1_Dense/config.json`` and
+    ``1_Dense/model.safetensors`` holding ``linear.weight`` [late_dim, hidden]
+    (no bias) in the model's storage dtype, the files libffwd/late.c:41-86
+    loads.  Weights N(0, 0.02^2) from their own seeded stream."""
+    dd = os.path.join(out_dir, "1_Dense")
+    os.makedirs(dd, exist_ok=True)
+    with open(os.path.join(dd, "config.json"), "w") as f:
+        json.dump({"in_features": s.hidden, "out_features": s.late_dim, "bias": False,
+                   "activation_function": "torch.nn.modules.linear.Identity"}, f, indent=1)
+    v = _gen(np.random.default_rng(s.seed + 7919), (s.late_dim, s.hidden), "w")
+    st_dt, data = ("BF16", f32_to_bf16_bits(v).tobytes()) if s.dtype == "bf16" else \
+        ("F32", v.astype(np.float32).tobytes())
+    hdr = _safetensors_header([("linear.weight", st_dt, (s.late_dim, s.hidden), 0, len(data))])
+    with open(os.path.join(dd, "model.safetensors"), "wb") as f:
+        f.write(struct.pack("<Q", len(hdr)))
+        f.write(hdr)
+        f.write(data)
+
+
 def _spec_key(s: ModelSpec) -> str:
-    return hashlib.sha1(json.dumps(asdict(s), sort_keys=True).encode()).hexdigest()[:12]
+    d = asdict(s)
+    if not d.get("late_dim"):
+        d.pop("late_dim", None)  # keys of pooled models predate the field
+    return hashlib.sha1(json.dumps(d, sort_keys=True).encode()).hexdigest()[:12]
 
 
 def ensure_model(s: ModelSpec, root: str | None = None) -> str:

@@ -96,6 +96,18 @@ typedef struct {
     const ffwd_span_t *spans;
     int n_spans;
 } ffwd_context_input_t;
+
+/* libffwd/ffwd.h:146-158 */
+typedef struct {
+    const int *query_ids;
+    int query_n_tokens;
+    int query_n_keep;
+    const int *const *doc_ids;
+    const int *doc_n_tokens;
+    const int *const *doc_keep;
+    const int *doc_n_keep;
+    int n_docs;
+} ffwd_rerank_input_t;
 #endif /* FFWD_H */
 
 typedef struct ffwd_b200_ctx ffwd_b200_ctx_t;
@@ -140,6 +152,43 @@ FFWD_B200_API int ffwd_b200_encode_batch(ffwd_b200_ctx_t *ctx, const ffwd_input_
 FFWD_B200_API int ffwd_b200_encode_spans_batch(ffwd_b200_ctx_t *ctx,
                                                const ffwd_context_input_t *inputs, int batch,
                                                float *out_embeddings);
+
+/* ---- Late interaction: mirror of libffwd/cuda.h:30-60 ----------------------- */
+
+typedef struct ffwd_b200_late_ctx ffwd_b200_late_ctx_t;
+
+/* Load a late-interaction model: base model + 1_Dense/model.safetensors
+ * `linear.weight` [token_dim, hidden] (token_dim <= 1024), on the first device
+ * of the device set.  NULL without a 1_Dense head or with a bad projection.
+ * Replaces ffwd_cuda_late_load (cuda.h:35; cuda.cu:5267-5296). */
+FFWD_B200_API ffwd_b200_late_ctx_t *ffwd_b200_late_load(const char *model_dir);
+/* Replaces ffwd_cuda_late_free (cuda.h:36). */
+FFWD_B200_API void ffwd_b200_late_free(ffwd_b200_late_ctx_t *ctx);
+/* Replaces ffwd_cuda_late_config (cuda.h:37). */
+FFWD_B200_API const ffwd_config_t *ffwd_b200_late_config(const ffwd_b200_late_ctx_t *ctx);
+/* Replaces ffwd_cuda_late_token_dim (cuda.h:38). */
+FFWD_B200_API int ffwd_b200_late_token_dim(const ffwd_b200_late_ctx_t *ctx);
+/* token_ids -> out_vectors[n_tokens * token_dim] (host), each vector the
+ * projection of the final hidden state (decoders: after the final RMSNorm),
+ * L2-normalised when `normalize`.  Replaces ffwd_cuda_late_encode_tokens
+ * (cuda.h:41-42; cuda.cu:5364-5384). */
+FFWD_B200_API int ffwd_b200_late_encode_tokens(ffwd_b200_late_ctx_t *ctx, const int *token_ids,
+                                               int n_tokens, int normalize, float *out_vectors);
+/* n_docs documents in one packed forward; document d's kept token vectors
+ * (rows keep[d][0..n_keep[d])) back to back in out_vectors, out_offsets[n_docs
+ * + 1] their prefix sum.  Replaces ffwd_cuda_late_encode_docs (cuda.h:50-58;
+ * cuda.cu:5386-5452); the gather and normalisation run on the device. */
+FFWD_B200_API int ffwd_b200_late_encode_docs(ffwd_b200_late_ctx_t *ctx, const int *const *doc_ids,
+                                             const int *n_tokens, const int *const *keep,
+                                             const int *n_keep, int n_docs, int normalize,
+                                             float *out_vectors, int *out_offsets);
+/* MaxSim scores of one query against n_docs candidates: query and candidates
+ * in one packed forward, normalised vectors and scores computed on the device,
+ * scores[n_docs] copied back.  Same result as the reference's ffwd_rerank
+ * (backend_cuda.c:132-156: encode_tokens + encode_docs + host
+ * ffwd_late_maxsim_batch, late.c:143-219). */
+FFWD_B200_API int ffwd_b200_late_rerank(ffwd_b200_late_ctx_t *ctx, const ffwd_rerank_input_t *in,
+                                        float *scores);
 
 /* ---- No counterpart in the reference ------------------------------------ */
 

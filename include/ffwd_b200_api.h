@@ -31,17 +31,7 @@ typedef struct {
     double memory_utilization;
 } ffwd_options_t;
 
-/* libffwd/ffwd.h:146-157 */
-typedef struct {
-    const int *query_ids;
-    int query_n_tokens;
-    int query_n_keep;
-    const int *const *doc_ids;
-    const int *doc_n_tokens;
-    const int *const *doc_keep;
-    const int *doc_n_keep;
-    int n_docs;
-} ffwd_rerank_input_t;
+/* ffwd_rerank_input_t (libffwd/ffwd.h:146-158) comes from ffwd_b200.h. */
 
 FFWD_B200_API int ffwd_init(const ffwd_options_t *opts, char *err, size_t errlen);
 FFWD_B200_API ffwd_t *ffwd_open(const char *model_dir, int is_late, const ffwd_options_t *opts,

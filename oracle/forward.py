@@ -316,3 +316,53 @@ class OracleModel:
                 emb = (np.sum(rows, 0, dtype=F32) * (F32(1.0) / F32(e - s))).astype(F32)
             out[b] = l2_normalize(emb) if c["normalize"] else emb
         return out
+
+
+# --------------------------------------------------------------------------- late interaction
+
+
+class OracleLate:
+    """Numpy late-interaction model: the base model's final hidden states (the
+    decoder's after its final RMSNorm, forward.c:470-490 with
+    apply_final_norm = 1), the 1_Dense projection (late.c:41-86, no bias), L2 per
+    vector (late_blas.c:57-85) and MaxSim (late.c:126-219).  The reference's CPU
+    path only runs decoder base models (ffwd_model_forward_into); for BERT
+    bases this restates the same steps over the BERT forward."""
+
+    def __init__(self, model_dir: str):
+        self.base = OracleModel(model_dir)
+        self.w = load_tensors(os.path.join(model_dir, "1_Dense"))["linear.weight"]
+        self.dim = int(self.w.shape[0])
+
+    def _vectors(self, seqs, rows, normalize):
+        x, _ = self.base.hidden_states(seqs)
+        c, t = self.base.cfg, self.base.t
+        if c["family"] != "bert":
+            x = rms_norm(x, t[self.base.p + "norm.weight"], c["rms_eps"])
+        v = (x[np.asarray(rows, np.int64)] @ self.w.T).astype(F32)
+        if normalize:
+            v = np.stack([l2_normalize(r) for r in v]) if len(v) else v
+        return v
+
+    def encode_tokens(self, ids, normalize=True):
+        return self._vectors([ids], np.arange(len(ids)), normalize)
+
+    def encode_docs(self, docs, keeps, normalize=True):
+        starts = np.concatenate([[0], np.cumsum([len(d) for d in docs])])
+        rows = np.concatenate([starts[i] + np.asarray(k, np.int64) for i, k in enumerate(keeps)])
+        offs = np.concatenate([[0], np.cumsum([len(k) for k in keeps])]).astype(np.int32)
+        return self._vectors(docs, rows, normalize), offs
+
+    @staticmethod
+    def maxsim_batch(q, docs, offs):
+        out = np.zeros(len(offs) - 1, dtype=F32)
+        for i in range(len(offs) - 1):
+            sim = q @ docs[offs[i]:offs[i + 1]].T
+            out[i] = np.sum(sim.max(axis=1), dtype=F32)
+        return out
+
+    def rerank(self, query, query_n_keep, docs, keeps):
+        """ffwd_rerank (backend_cuda.c:132-156)."""
+        qv = self.encode_tokens(query, True)[:query_n_keep]
+        dv, offs = self.encode_docs(docs, keeps, True)
+        return self.maxsim_batch(qv, dv, offs)

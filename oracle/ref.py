@@ -33,6 +33,17 @@ def lib():
         l.ref_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                  ctypes.c_void_p]
         l.ref_forward.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        l.ref_late_load.restype = ctypes.c_void_p
+        l.ref_late_load.argtypes = [ctypes.c_char_p]
+        l.ref_late_free.argtypes = [ctypes.c_void_p]
+        l.ref_late_token_dim.argtypes = [ctypes.c_void_p]
+        l.ref_late_encode_tokens.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                             ctypes.c_int, ctypes.c_void_p]
+        l.ref_late_encode_docs.argtypes = [ctypes.c_void_p] + [ctypes.c_void_p] * 4 + [
+            ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        l.ref_late_maxsim_batch.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_void_p]
         _lib = l
     return _lib
 
@@ -72,6 +83,66 @@ class RefModel:
     def close(self):
         if self.h:
             self.l.ref_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class RefLate:
+    """The reference's CPU late-interaction model (libffwd/late.c, late_blas.c)."""
+
+    def __init__(self, model_dir: str, threads: int = 1):
+        self.l = lib()
+        self.l.ref_set_threads(int(threads))
+        self.h = self.l.ref_late_load(model_dir.encode())
+        if not self.h:
+            raise RuntimeError(f"reference failed to load late model {model_dir}")
+        self.dim = int(self.l.ref_late_token_dim(self.h))
+
+    def encode_tokens(self, ids, normalize=True) -> np.ndarray:
+        ids = np.ascontiguousarray(np.asarray(ids, np.int32))
+        out = np.zeros((len(ids), self.dim), np.float32)
+        if self.l.ref_late_encode_tokens(self.h, ids.ctypes.data, len(ids), int(normalize),
+                                         out.ctypes.data) != 0:
+            raise RuntimeError("reference late encode_tokens failed")
+        return out
+
+    def encode_docs(self, docs, keeps, normalize=True):
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(d, np.int32) for d in docs]))
+        lens = np.ascontiguousarray(np.array([len(d) for d in docs], np.int32))
+        keep = np.ascontiguousarray(np.concatenate([np.asarray(k, np.int32) for k in keeps]))
+        nk = np.ascontiguousarray(np.array([len(k) for k in keeps], np.int32))
+        out = np.zeros((int(nk.sum()), self.dim), np.float32)
+        offs = np.zeros(len(docs) + 1, np.int32)
+        if self.l.ref_late_encode_docs(self.h, ids.ctypes.data, lens.ctypes.data, keep.ctypes.data,
+                                       nk.ctypes.data, len(docs), int(normalize), out.ctypes.data,
+                                       offs.ctypes.data) != 0:
+            raise RuntimeError("reference late encode_docs failed")
+        return out, offs
+
+    def maxsim_batch(self, q, docs, offs) -> np.ndarray:
+        q = np.ascontiguousarray(q, np.float32)
+        docs = np.ascontiguousarray(docs, np.float32)
+        offs = np.ascontiguousarray(offs, np.int32)
+        scores = np.zeros(len(offs) - 1, np.float32)
+        if self.l.ref_late_maxsim_batch(q.ctypes.data, len(q), docs.ctypes.data, offs.ctypes.data,
+                                        len(offs) - 1, q.shape[1], scores.ctypes.data) != 0:
+            raise RuntimeError("reference maxsim failed")
+        return scores
+
+    def rerank(self, query, query_n_keep, docs, keeps) -> np.ndarray:
+        """The reference's ffwd_rerank (backend_cuda.c:132-156) on its CPU path."""
+        qv = self.encode_tokens(query, True)
+        dv, offs = self.encode_docs(docs, keeps, True)
+        return self.maxsim_batch(qv[:query_n_keep], dv, offs)
+
+    def close(self):
+        if self.h:
+            self.l.ref_late_free(self.h)
             self.h = None
 
     def __del__(self):

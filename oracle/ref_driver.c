@@ -97,3 +97,77 @@ ref_forward(void *p, const int *ids, int n, float *out_states) {
     ref_handle_t *h = p;
     return ffwd_model_forward_into(h->model, h->ws, ids, n, out_states);
 }
+
+/* ---- late interaction: the reference's CPU late model (libffwd/late.c,
+ * late_blas.c), called as its MLX/BLAS backends do. */
+
+typedef struct {
+    ffwd_late_model_t *model;
+    ffwd_late_workspace_t *ws;
+} ref_late_t;
+
+__attribute__((visibility("default"))) void *ref_late_load(const char *dir) {
+    ref_late_t *h = calloc(1, sizeof(*h));
+    if (!h)
+        return NULL;
+    h->model = ffwd_late_model_load(dir);
+    if (!h->model || !(h->ws = ffwd_late_workspace_new(h->model))) {
+        ffwd_late_model_free(h->model);
+        free(h);
+        return NULL;
+    }
+    return h;
+}
+
+__attribute__((visibility("default"))) void ref_late_free(void *p) {
+    ref_late_t *h = p;
+    if (!h)
+        return;
+    ffwd_late_workspace_free(h->ws);
+    ffwd_late_model_free(h->model);
+    free(h);
+}
+
+__attribute__((visibility("default"))) int ref_late_token_dim(void *p) {
+    return ffwd_late_model_token_dim(((ref_late_t *)p)->model);
+}
+
+__attribute__((visibility("default"))) int
+ref_late_encode_tokens(void *p, const int *ids, int n, int normalize, float *out) {
+    ref_late_t *h = p;
+    return ffwd_late_model_encode_tokens(h->model, h->ws, ids, n, normalize, out);
+}
+
+/* Documents concatenated: ids / lens[n_docs]; kept indices concatenated:
+ * keep / n_keep[n_docs]. */
+__attribute__((visibility("default"))) int
+ref_late_encode_docs(void *p, const int *ids, const int *lens, const int *keep, const int *n_keep,
+                     int n_docs, int normalize, float *out, int *out_offsets) {
+    ref_late_t *h = p;
+    const int **doc_ids = malloc((size_t)n_docs * sizeof(*doc_ids));
+    const int **keeps = malloc((size_t)n_docs * sizeof(*keeps));
+    if (!doc_ids || !keeps) {
+        free(doc_ids);
+        free(keeps);
+        return -1;
+    }
+    size_t oi = 0, ok = 0;
+    for (int d = 0; d < n_docs; d++) {
+        doc_ids[d] = ids + oi;
+        keeps[d] = keep + ok;
+        oi += (size_t)lens[d];
+        ok += (size_t)n_keep[d];
+    }
+    int rc = ffwd_late_model_encode_docs(h->model, h->ws, (const int *const *)doc_ids, lens,
+                                         (const int *const *)keeps, n_keep, n_docs, normalize, out,
+                                         out_offsets);
+    free(doc_ids);
+    free(keeps);
+    return rc;
+}
+
+__attribute__((visibility("default"))) int
+ref_late_maxsim_batch(const float *q, int nq, const float *docs, const int *offsets, int n_docs,
+                      int dim, float *scores) {
+    return ffwd_late_maxsim_batch(q, nq, docs, offsets, n_docs, dim, scores);
+}

@@ -4,7 +4,10 @@ Each fixture holds a seeded synthetic model spec (the model is regenerated
 bit-identically by ``ffwd_b200.synth.write_model``), a packed token batch and
 the embeddings the reference's own CPU path (``oracle/_ref/libffwd_ref.so``,
 built from the unmodified reference sources by ``oracle/Makefile``) returns
-for it through ``ffwd_model_encode_batch``.
+for it through ``ffwd_model_encode_batch``.  ``late/*.npz`` hold late-interaction
+cases: a query, candidate documents and kept-token lists, with the reference's
+``ffwd_late_model_encode_tokens`` / ``_encode_docs`` vectors and
+``ffwd_late_maxsim_batch`` scores (the steps of ``ffwd_rerank``).
 
     python tests/golden/make_golden.py    (needs oracle/_ref, i.e. `make -C oracle`)
 """
@@ -23,7 +26,7 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(HERE))
 
 from ffwd_b200 import synth  # noqa: E402
-from oracle.ref import RefModel  # noqa: E402
+from oracle.ref import RefLate, RefModel  # noqa: E402
 from helpers import small_spec, small_batch  # noqa: E402
 
 CASES = {
@@ -38,6 +41,44 @@ CASES = {
     "bert_tanh_cls": ("bert-tanh-1l", lambda: small_batch("bert-tanh-1l", n=4)),
     "qwen3_bidir": ("qwen3-bidir-1l", lambda: small_batch("qwen3-bidir-1l", n=3, max_len=140)),
 }
+
+
+LATE_CASES = {
+    # name: (small spec key, query length, query_n_keep, doc lengths, seed)
+    "qwen3_late_bf16": ("qwen3-late-2l", 24, 20, (60, 131, 9, 257), 3),
+    "qwen3_late_f32": ("qwen3-late-f32-1l", 11, 11, (5, 40, 1), 4),
+}
+
+
+def late_case(spec, q_len, q_keep, doc_lens, seed):
+    rng = np.random.default_rng(seed)
+    hi = min(spec.vocab - 1, 151642)
+    query = rng.integers(0, hi, q_len).astype(np.int32)
+    docs = [rng.integers(0, hi, n).astype(np.int32) for n in doc_lens]
+    keeps = [np.sort(rng.choice(n, size=max(1, (3 * n) // 4), replace=False)).astype(np.int32)
+             for n in doc_lens]
+    return query, q_keep, docs, keeps
+
+
+def main_late(root):
+    os.makedirs(os.path.join(HERE, "late"), exist_ok=True)
+    for name, (key, q_len, q_keep, doc_lens, seed) in LATE_CASES.items():
+        s = small_spec(key)
+        d = synth.ensure_model(s, root)
+        query, qk, docs, keeps = late_case(s, q_len, q_keep, doc_lens, seed)
+        ref = RefLate(d, threads=os.cpu_count() or 1)
+        q_vec = ref.encode_tokens(query, True)
+        q_raw = ref.encode_tokens(query, False)
+        d_vec, d_off = ref.encode_docs(docs, keeps, True)
+        scores = ref.maxsim_batch(q_vec[:qk], d_vec, d_off)
+        ref.close()
+        np.savez_compressed(
+            os.path.join(HERE, "late", f"{name}.npz"),
+            spec=json.dumps(dataclasses.asdict(s)), query=query, query_n_keep=np.int32(qk),
+            doc_ids=np.concatenate(docs), doc_lens=np.array(doc_lens, np.int32),
+            keep=np.concatenate(keeps), n_keep=np.array([len(k) for k in keeps], np.int32),
+            q_vec=q_vec, q_raw=q_raw, d_vec=d_vec, d_off=d_off, scores=scores)
+        print(name, q_vec.shape, d_vec.shape, scores)
 
 
 def main():
@@ -57,6 +98,7 @@ def main():
             expected=out.astype(np.float32),
         )
         print(name, out.shape)
+    main_late(root)
 
 
 if __name__ == "__main__":

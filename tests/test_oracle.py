@@ -2,6 +2,9 @@
 reference's own CPU path, the compiled reference itself (when built), and the
 reference's kernel known-answer values (tests/test_kernels.c:96-127)."""
 
+import json
+import os
+
 import numpy as np
 import pytest
 
@@ -70,3 +73,28 @@ def test_oracle_rejects_bad_inputs(model_root):
         m.encode_batch([np.zeros(0, np.int32)])
     with pytest.raises(ValueError):
         m.encode_batch([np.full(600, 1000, np.int32)])
+
+
+LATE_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "late")
+
+
+@pytest.mark.parametrize("name", sorted(os.path.splitext(f)[0] for f in os.listdir(LATE_DIR)
+                                        if f.endswith(".npz")))
+def test_late_oracle_matches_reference_golden(name, model_root):
+    """The numpy late-interaction restatement against the reference's own CPU
+    late path (ffwd_late_model_encode_tokens / _encode_docs / maxsim_batch)."""
+    z = np.load(os.path.join(LATE_DIR, name + ".npz"))
+    spec = synth.ModelSpec(**json.loads(str(z["spec"])))
+    d = synth.ensure_model(spec, model_root)
+    lo = np.concatenate([[0], np.cumsum(z["doc_lens"])])
+    ko = np.concatenate([[0], np.cumsum(z["n_keep"])])
+    docs = [z["doc_ids"][lo[i]:lo[i + 1]] for i in range(len(lo) - 1)]
+    keeps = [z["keep"][ko[i]:ko[i + 1]] for i in range(len(ko) - 1)]
+    o = of.OracleLate(d)
+    assert np.abs(o.encode_tokens(z["query"], True) - z["q_vec"]).max() <= 1e-5
+    assert np.abs(o.encode_tokens(z["query"], False) - z["q_raw"]).max() <= 1e-4
+    dv, do = o.encode_docs(docs, keeps, True)
+    assert np.array_equal(do, z["d_off"])
+    assert np.abs(dv - z["d_vec"]).max() <= 1e-5
+    sc = o.maxsim_batch(z["q_vec"][:int(z["query_n_keep"])], z["d_vec"], z["d_off"])
+    assert np.abs(sc - z["scores"]).max() <= 1e-4
