@@ -868,10 +868,19 @@ int check_err(Device &D) {
     return 0;
 }
 
+// Output form of pooled rows: the first `dims` values (L2-renormalised when
+// `renorm`) as f32, tanh-int8 or sign bits (encode_rows_launch); row_bytes per
+// output row.
+struct OutSpec {
+    int dims = 0, renorm = 0, enc = 0;
+    size_t row_bytes = 0;
+};
+
 // Encode the sequences idx[] of inputs on device D (as one or more forwards of
-// at most g_max_tokens packed rows), writing pooled rows to out[idx[i]].
+// at most g_max_tokens packed rows), writing output rows to out + idx[i] *
+// os.row_bytes.
 int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
-                  const std::vector<int> &idx, float *out) {
+                  const std::vector<int> &idx, void *out, const OutSpec &os) {
     const ffwd_config_t &c = ctx->cfg;
     const int H = c.hidden_size;
     CK(cudaSetDevice(D.dev));
@@ -917,12 +926,24 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
         LAUNCH(pool_launch(w.x, w.offsets, B, H, c.pooling_mode,
                            c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm, c.rms_norm_eps,
                            c.normalize_embeddings, w.pooled, w.err, D.stream));
-        CK(cudaMemcpyAsync(w.h_out, w.pooled, (size_t)B * H * 4, cudaMemcpyDeviceToHost, D.stream));
+        const void *src = w.pooled;
+        if (os.enc != 0 || os.dims != H || os.renorm) {
+            // The FFN activation buffer is free after the forward: T >= B rows
+            // of intermediate_size bf16 values, at least the 4 * H bytes of an
+            // f32 row (intermediate_size >= 2 * hidden in every supported model).
+            LAUNCH(encode_rows_launch(w.pooled, B, H, os.dims, os.renorm, os.enc, w.hmid, w.err,
+                                      D.stream));
+            src = w.hmid;
+        }
+        CK(cudaMemcpyAsync(w.h_out, src, (size_t)B * os.row_bytes, cudaMemcpyDeviceToHost,
+                           D.stream));
         CK(cudaMemcpyAsync(w.h_err, w.err, 4, cudaMemcpyDeviceToHost, D.stream));
         CK(cudaStreamSynchronize(D.stream));
         if (check_err(D)) return -1;
         for (int b = 0; b < B; ++b)
-            memcpy(out + (size_t)idx[i0 + b] * H, w.h_out + (size_t)b * H, (size_t)H * 4);
+            memcpy(static_cast<uint8_t *>(out) + (size_t)idx[i0 + b] * os.row_bytes,
+                   reinterpret_cast<const uint8_t *>(w.h_out) + (size_t)b * os.row_bytes,
+                   os.row_bytes);
         i0 = i1;
     }
     return 0;
@@ -1165,18 +1186,18 @@ FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts
     return 0;
 }
 
-FFWD_B200_API int ffwd_b200_encode_batch(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs,
-                                         int batch, float *out) {
-    t_err.clear();
-    if (!out || validate_inputs(ctx, inputs, batch)) {
-        if (!out) fail("null output");
-        return -1;
-    }
+}  // extern "C"
+
+namespace fb {
+namespace {
+
+int encode_batch_impl(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs, int batch, void *out,
+                      const OutSpec &os) {
     const int nd = (int)ctx->devs.size();
     if (nd == 1) {
         std::vector<int> idx(batch);
         std::iota(idx.begin(), idx.end(), 0);
-        return run_on_device(ctx, ctx->devs[0], inputs, idx, out);
+        return run_on_device(ctx, ctx->devs[0], inputs, idx, out, os);
     }
     std::vector<double> cost(batch);
     for (int b = 0; b < batch; ++b) cost[b] = seq_cost(ctx, inputs[b].n_tokens);
@@ -1190,7 +1211,7 @@ FFWD_B200_API int ffwd_b200_encode_batch(ffwd_b200_ctx_t *ctx, const ffwd_input_
     for (int d = 0; d < nd; ++d) {
         if (idx[d].empty()) continue;
         th.emplace_back([&, d] {
-            rc[d] = run_on_device(ctx, ctx->devs[d], inputs, idx[d], out);
+            rc[d] = run_on_device(ctx, ctx->devs[d], inputs, idx[d], out, os);
             errs[d] = t_err;
         });
     }
@@ -1201,6 +1222,44 @@ FFWD_B200_API int ffwd_b200_encode_batch(ffwd_b200_ctx_t *ctx, const ffwd_input_
             return -1;
         }
     return 0;
+}
+
+}  // namespace
+}  // namespace fb
+
+extern "C" {
+
+FFWD_B200_API int ffwd_b200_encode_batch(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs,
+                                         int batch, float *out) {
+    t_err.clear();
+    if (!out || validate_inputs(ctx, inputs, batch)) {
+        if (!out) fail("null output");
+        return -1;
+    }
+    const int H = ctx->cfg.hidden_size;
+    return encode_batch_impl(ctx, inputs, batch, out, OutSpec{H, 0, 0, (size_t)H * 4});
+}
+
+FFWD_B200_API int ffwd_b200_encode_batch_as(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs,
+                                            int batch, int dims, int renormalize, int encoding,
+                                            void *out) {
+    t_err.clear();
+    if (!out || validate_inputs(ctx, inputs, batch)) {
+        if (!out) fail("null output");
+        return -1;
+    }
+    const int H = ctx->cfg.hidden_size;
+    if (dims <= 0 || dims > H || encoding < FFWD_B200_OUT_F32 || encoding > FFWD_B200_OUT_BINARY ||
+        (encoding == FFWD_B200_OUT_BINARY && dims % 8 != 0)) {
+        fail("invalid output form: dims %d (1..%d, a multiple of 8 for binary), encoding %d",
+             dims, H, encoding);
+        return -1;
+    }
+    const size_t row = encoding == FFWD_B200_OUT_F32    ? (size_t)dims * 4
+                       : encoding == FFWD_B200_OUT_INT8 ? (size_t)dims
+                                                        : (size_t)dims / 8;
+    return encode_batch_impl(ctx, inputs, batch, out,
+                             OutSpec{dims, renormalize && dims < H ? 1 : 0, encoding, row});
 }
 
 FFWD_B200_API int ffwd_b200_encode_into(ffwd_b200_ctx_t *ctx, const int *ids, int n, float *out) {

@@ -281,6 +281,57 @@ __global__ void __launch_bounds__(kPoolThreads)
     }
 }
 
+constexpr int kEncThreads = 128;
+
+// One CTA per pooled row.
+__global__ void __launch_bounds__(kEncThreads)
+    encode_rows_kernel(const float *emb, int H, int dims, int renorm, int enc, void *out,
+                       int *err) {
+    __shared__ float red[kEncThreads / 32];
+    __shared__ float inv_sh;
+    const int b = blockIdx.x;
+    const float *e = emb + (size_t)b * H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (renorm) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < dims; i += kEncThreads) ss += e[i] * e[i];
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float t = 0.0f;
+            for (int w = 0; w < kEncThreads / 32; ++w) t += red[w];
+            if (!(t > 0.0f) || !isfinite(t)) {
+                set_error(err, kErrBadNorm);
+                t = 1.0f;
+            }
+            inv_sh = 1.0f / sqrtf(t);
+        }
+        __syncthreads();
+    }
+    const float inv = renorm ? inv_sh : 1.0f;
+    if (enc == 0) {
+        float *o = static_cast<float *>(out) + (size_t)b * dims;
+        for (int i = threadIdx.x; i < dims; i += kEncThreads) o[i] = e[i] * inv;
+    } else if (enc == 1) {
+        int8_t *o = static_cast<int8_t *>(out) + (size_t)b * dims;
+        for (int i = threadIdx.x; i < dims; i += kEncThreads) {
+            int v = __float2int_rn(tanhf(e[i] * inv) * 127.0f);
+            o[i] = (int8_t)(v > 127 ? 127 : (v < -128 ? -128 : v));
+        }
+    } else {
+        // 32 values per warp step: bit i of the ballot is value base + i, so
+        // its bytes are the wire bytes in order (dims is a multiple of 8).
+        uint8_t *o = static_cast<uint8_t *>(out) + (size_t)b * (dims / 8);
+        for (int base = warp * 32; base < dims; base += kEncThreads) {
+            const int i = base + lane;
+            const unsigned m = __ballot_sync(0xffffffffu, i < dims && e[i] * inv >= 0.0f);
+            const int nbytes = min(4, (dims - base) / 8);
+            if (lane < nbytes) o[base / 8 + lane] = (uint8_t)(m >> (8 * lane));
+        }
+    }
+}
+
 inline int row_blocks(int T) { return (T + kRowWarps - 1) / kRowWarps; }
 
 }  // namespace
@@ -332,6 +383,15 @@ int pool_launch(const float *x, const int *offsets, int batch, int H, int mode,
     if (H > kPoolThreads * kPoolMaxCols) return cudaErrorInvalidValue;
     pool_kernel<<<batch, kPoolThreads, 0, s>>>(x, offsets, offsets + 1, H, mode, norm_w, eps,
                                                 normalize, out, err);
+    return cudaGetLastError();
+}
+
+int encode_rows_launch(const float *emb, int B, int H, int dims, int renorm, int enc, void *out,
+                       int *err, cudaStream_t s) {
+    if (B <= 0) return cudaSuccess;
+    if (dims <= 0 || dims > H || enc < 0 || enc > 2 || (enc == 2 && dims % 8 != 0))
+        return cudaErrorInvalidValue;
+    encode_rows_kernel<<<B, kEncThreads, 0, s>>>(emb, H, dims, renorm, enc, out, err);
     return cudaGetLastError();
 }
 

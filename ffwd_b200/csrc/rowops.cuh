@@ -50,4 +50,13 @@ int pool_launch(const float *x, const int *offsets, int batch, int H, int mode,
 int span_pool_launch(const float *x, const int *starts, const int *ends, int n_spans, int H,
                      const float *norm_w, float eps, float *out, cudaStream_t s);
 
+// Output encodings of pooled embeddings emb [B, H] (server wire forms,
+// tools/server/encode.c:20-61, 107-122): the first `dims` values, L2-renormalised
+// when `renorm` (Matryoshka truncation), then enc 0: f32 [B, dims]; enc 1:
+// int8 round(tanh(x) * 127) clamped to [-128, 127], [B, dims]; enc 2: one bit
+// per value (x >= 0), 8 per byte least significant first, [B, dims / 8].
+// A zero / non-finite truncated norm records kErrBadNorm.
+int encode_rows_launch(const float *emb, int B, int H, int dims, int renorm, int enc, void *out,
+                       int *err, cudaStream_t s);
+
 }  // namespace fb

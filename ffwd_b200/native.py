@@ -96,6 +96,9 @@ ABI = {
     "ffwd_b200_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                            ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "ffwd_b200_encode_batch_as": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                 ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_void_p]),
     "ffwd_b200_late_load": (ctypes.c_void_p, [ctypes.c_char_p]),
     "ffwd_b200_late_free": (None, [ctypes.c_void_p]),
     "ffwd_b200_late_config": (ctypes.POINTER(ffwd_config_t), [ctypes.c_void_p]),
@@ -215,6 +218,20 @@ class B200Model:
         rc = self._l.ffwd_b200_encode_batch(self.h, ins, len(seqs), out.ctypes.data)
         if rc != 0:
             raise FfwdError(f"encode_batch failed: {last_error()}")
+        return out
+
+    ENCODINGS = {"f32": (0, np.float32), "int8": (1, np.int8), "binary": (2, np.uint8)}
+
+    def encode_batch_as(self, seqs, dims: int, renormalize: bool, encoding: str) -> np.ndarray:
+        """Embeddings in a wire form made on the device: f32 [n, dims], int8
+        [n, dims] or binary [n, dims / 8] bytes."""
+        enc, dt = self.ENCODINGS[encoding]
+        ins, keep = _pack_inputs(seqs)
+        width = dims // 8 if encoding == "binary" else dims
+        out = np.zeros((len(seqs), max(width, 1)), dtype=dt)
+        if self._l.ffwd_b200_encode_batch_as(self.h, ins, len(seqs), int(dims), int(renormalize),
+                                             enc, out.ctypes.data) != 0:
+            raise FfwdError(f"encode_batch_as failed: {last_error()}")
         return out
 
     def try_encode_batch(self, seqs):

@@ -192,6 +192,25 @@ FFWD_B200_API int ffwd_b200_late_rerank(ffwd_b200_late_ctx_t *ctx, const ffwd_re
 
 /* ---- No counterpart in the reference ------------------------------------ */
 
+/* Output encodings of ffwd_b200_encode_batch_as. */
+enum {
+    FFWD_B200_OUT_F32 = 0,  /* float32 [batch * dims] */
+    FFWD_B200_OUT_INT8 = 1, /* int8 round(tanh(x) * 127), clamped [batch * dims] */
+    FFWD_B200_OUT_BINARY = 2 /* sign bits (x >= 0), 8 per byte, least significant bit first
+                                [batch * dims / 8] */
+};
+
+/* ffwd_b200_encode_batch with the embedding's wire form produced on the device:
+ * the first `dims` (1..hidden) values of each pooled embedding, L2-renormalised
+ * when `renormalize` and dims < hidden (Matryoshka truncation), then encoded.
+ * The reference's server applies the same steps to host floats
+ * (tools/server/encode.c:20-61 quantize_int8_tanh / base64_binary, 107-122
+ * truncate + renormalise); doing them on the device shrinks the copy back to
+ * 1/4 (int8) or 1/32 (binary).  Binary needs dims % 8 == 0.  0 / -1. */
+FFWD_B200_API int ffwd_b200_encode_batch_as(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs,
+                                            int batch, int dims, int renormalize, int encoding,
+                                            void *out);
+
 /* Device set used by the next ffwd_b200_load (replicated weights, sequences
  * sharded by LPT over estimated cost).  Default: $FFWD_B200_DEVICES
  * ("0,1,..."), else device 0. */

@@ -366,3 +366,23 @@ class OracleLate:
         qv = self.encode_tokens(query, True)[:query_n_keep]
         dv, offs = self.encode_docs(docs, keeps, True)
         return self.maxsim_batch(qv, dv, offs)
+
+
+
+# --------------------------------------------------------------------------- output encodings
+
+
+def quantize_int8_tanh(x):
+    """tools/server/encode.c:20-27: lrintf(tanhf(x) * 127) clamped to [-128, 127]."""
+    v = np.rint(np.tanh(np.asarray(x, F32)).astype(F32) * F32(127.0))
+    return np.clip(v, -128, 127).astype(np.int8)
+
+
+def binary_bits(x):
+    """tools/server/encode.c:42-51: bit i = (x[i] >= 0), bits[i >> 3] |= 1 << (i & 7)."""
+    return np.packbits(np.asarray(x) >= 0, axis=-1, bitorder="little")
+
+
+def truncate_renormalize(emb, dims):
+    """tools/server/encode.c:107-122: first dims values, then ffwd_l2_normalize."""
+    return np.stack([l2_normalize(r[:dims].astype(F32)) for r in np.atleast_2d(emb)])

@@ -196,3 +196,29 @@ def test_multi_device_sharding_matches_single(model_root):
     native.lib().ffwd_b200_set_devices((ctypes.c_int * 1)(0), 1)
     # Every sequence is computed identically on whichever device gets it.
     assert np.array_equal(single, multi)
+
+
+@pytest.mark.parametrize("key,mode", [("qwen3-2l", "bf16"), ("minilm-2l", "f32")])
+def test_output_encodings(key, mode, model_root):
+    """ffwd_b200_encode_batch_as: the server's wire forms (tools/server/encode.c)
+    made on the device from the same pooled embeddings."""
+    s = small_spec(key)
+    d = synth.ensure_model(s, model_root)
+    m = model(d, mode)
+    seqs = small_batch(key, n=5, max_len=200)
+    H = m.hidden
+    full = m.encode_batch(seqs)
+    assert np.array_equal(m.encode_batch_as(seqs, H, False, "f32"), full)
+    q = m.encode_batch_as(seqs, H, False, "int8").astype(np.int32)
+    diff = np.abs(q - of.quantize_int8_tanh(full).astype(np.int32))
+    assert diff.max() <= 1 and (diff != 0).mean() <= 1e-3  # tanhf ulp at rounding ties only
+    assert np.array_equal(m.encode_batch_as(seqs, H, False, "binary"), of.binary_bits(full))
+    dims = H // 4
+    t = m.encode_batch_as(seqs, dims, True, "f32")
+    assert np.abs(t - of.truncate_renormalize(full, dims)).max() <= 1e-6
+    assert np.array_equal(m.encode_batch_as(seqs, dims, True, "binary"),
+                          of.binary_bits(full[:, :dims]))
+    assert np.array_equal(m.encode_batch_as(seqs, dims, False, "f32"), full[:, :dims])
+    for bad in ((0, "f32"), (H + 1, "f32"), (12, "binary")):
+        with pytest.raises(native.FfwdError):
+            m.encode_batch_as(seqs, bad[0], True, bad[1])

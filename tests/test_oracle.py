@@ -98,3 +98,15 @@ def test_late_oracle_matches_reference_golden(name, model_root):
     assert np.abs(dv - z["d_vec"]).max() <= 1e-5
     sc = o.maxsim_batch(z["q_vec"][:int(z["query_n_keep"])], z["d_vec"], z["d_off"])
     assert np.abs(sc - z["scores"]).max() <= 1e-4
+
+
+def test_output_encodings_known_values():
+    """tools/server/encode.c:20-51 wire forms."""
+    x = np.array([0.0, 10.0, -10.0, 0.5, -0.5, 1e-9, -1e-9], np.float32)
+    q = of.quantize_int8_tanh(x)
+    assert q.tolist() == [0, 127, -127, 59, -59, 0, 0]
+    bits = of.binary_bits(np.array([1, -1, 0, -0.5, 2, 3, -4, 5, -1, 1, -1, -1, -1, -1, -1, -1],
+                                   np.float32))
+    assert bits.tolist() == [0b10110101, 0b00000010]
+    e = of.truncate_renormalize(np.array([[3.0, 4.0, 12.0]], np.float32), 2)
+    assert np.allclose(e, [[0.6, 0.8]])
