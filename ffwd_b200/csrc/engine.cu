@@ -212,6 +212,15 @@ struct Device {
     int *h_late_rows = nullptr, *h_late_doff = nullptr;
     float *h_late_vec = nullptr, *h_late_scores = nullptr;
     size_t late_cap_rows = 0, late_cap_docs = 0;
+    // Second set of pinned host staging buffers, so the host packs (and
+    // launches) forward k + 1 of a long batch while the GPU runs forward k.
+    struct Staging {
+        int *ids = nullptr, *offsets = nullptr, *err = nullptr;
+        AttnItem *items = nullptr;
+        uint8_t *out = nullptr;
+        size_t cap_ids = 0, cap_off = 0, cap_items = 0, cap_out = 0;
+    } stg;
+    cudaEvent_t fwd_done[2] = {nullptr, nullptr};
 };
 
 }  // namespace
@@ -536,9 +545,12 @@ void free_device(Device &D) {
     void *lptrs[] = {D.late_wt, D.late_vec, D.late_rows, D.late_doff, D.late_scores};
     for (void *q : lptrs)
         if (q) cudaFree(q);
-    void *lhptrs[] = {D.h_late_rows, D.h_late_doff, D.h_late_vec, D.h_late_scores};
+    void *lhptrs[] = {D.h_late_rows, D.h_late_doff, D.h_late_vec, D.h_late_scores,
+                      D.stg.ids, D.stg.offsets, D.stg.err, D.stg.items, D.stg.out};
     for (void *q : lhptrs)
         if (q) cudaFreeHost(q);
+    for (cudaEvent_t e : D.fwd_done)
+        if (e) cudaEventDestroy(e);
     if (D.stream) cudaStreamDestroy(D.stream);
     D = Device();
 }
@@ -876,13 +888,34 @@ struct OutSpec {
     size_t row_bytes = 0;
 };
 
+// Pinned staging of one forward: ids, row offsets, attention items, output
+// rows and the error word.
+struct HostSet {
+    int *ids, *offsets, *err;
+    AttnItem *items;
+    uint8_t *out;
+};
+
+int grow_pinned(void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return 0;
+    if (*p) CK(cudaFreeHost(*p));
+    *p = nullptr;
+    *cap = 0;
+    CK(cudaMallocHost(p, need));
+    *cap = need;
+    return 0;
+}
+
 // Encode the sequences idx[] of inputs on device D (as one or more forwards of
 // at most g_max_tokens packed rows), writing output rows to out + idx[i] *
-// os.row_bytes.
+// os.row_bytes.  With several forwards, two pinned staging sets alternate:
+// forward k + 1 is packed and enqueued before the host waits for forward k,
+// so the host's packing, work-list building and launches overlap the GPU.
 int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
                   const std::vector<int> &idx, void *out, const OutSpec &os) {
     const ffwd_config_t &c = ctx->cfg;
     const int H = c.hidden_size;
+    const bool split = ctx->prec != 0;
     CK(cudaSetDevice(D.dev));
     // Forwards of at most g_max_tokens rows, sized evenly: with n forwards
     // needed, each aims at total / n tokens, so no small tail forward runs
@@ -891,8 +924,14 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
     for (int i : idx) total += inputs[i].n_tokens;
     const long long n_fwd = (total + g_max_tokens - 1) / g_max_tokens;
     const long long aim = n_fwd > 1 ? (total + n_fwd - 1) / n_fwd : total;
-    size_t i0 = 0;
-    while (i0 < idx.size()) {
+    struct Chunk {
+        size_t i0, i1;
+        int T, B;
+    };
+    std::vector<Chunk> chunks;
+    int maxT = 0, maxB = 0, maxItems = 0;
+    std::vector<int> offs;
+    for (size_t i0 = 0; i0 < idx.size();) {
         size_t i1 = i0;
         long long tok = 0;
         while (i1 < idx.size() &&
@@ -901,29 +940,79 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
             ++i1;
         }
         const int B = (int)(i1 - i0), T = (int)tok;
-        if (ensure_ws(ctx, D, T, B, 0, 0)) return -1;
-        Workspace &w = D.ws;
+        offs.assign(1, 0);
+        for (size_t i = i0; i < i1; ++i) offs.push_back(offs.back() + inputs[idx[i]].n_tokens);
+        const int n_items = attention_count_items(!split, c.n_heads, c.n_kv_heads, c.head_dim,
+                                                  offs.data(), B);
+        if (n_items < 0) {
+            fail("attention work list too large");
+            return -1;
+        }
+        chunks.push_back(Chunk{i0, i1, T, B});
+        maxT = std::max(maxT, T);
+        maxB = std::max(maxB, B);
+        maxItems = std::max(maxItems, n_items);
+        i0 = i1;
+    }
+    if (ensure_ws(ctx, D, maxT, maxB, maxItems, 0)) return -1;
+    Workspace &w = D.ws;
+    const HostSet set_a{w.h_ids, w.h_offsets, w.h_err, w.h_items, reinterpret_cast<uint8_t *>(w.h_out)};
+    HostSet sets[2] = {set_a, set_a};
+    if (chunks.size() > 1) {
+        auto &g = D.stg;
+        if (grow_pinned((void **)&g.ids, &g.cap_ids, (size_t)maxT * 4) ||
+            grow_pinned((void **)&g.offsets, &g.cap_off, (size_t)(maxB + 1) * 4) ||
+            grow_pinned((void **)&g.items, &g.cap_items, (size_t)maxItems * sizeof(AttnItem)) ||
+            grow_pinned((void **)&g.out, &g.cap_out, (size_t)maxB * os.row_bytes))
+            return -1;
+        if (!g.err) CK(cudaMallocHost(&g.err, 16));
+        for (auto &e : D.fwd_done)
+            if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        sets[1] = HostSet{g.ids, g.offsets, g.err, g.items, g.out};
+    }
+    auto use = [&](const HostSet &h) {
+        w.h_ids = h.ids;
+        w.h_offsets = h.offsets;
+        w.h_err = h.err;
+        w.h_items = h.items;
+        w.h_out = reinterpret_cast<float *>(h.out);
+    };
+    // Copy forward k's rows out once its stream work is done.
+    auto finish = [&](size_t k) -> int {
+        const HostSet &h = sets[k & 1];
+        if (chunks.size() > 1) CK(cudaEventSynchronize(D.fwd_done[k & 1]));
+        else CK(cudaStreamSynchronize(D.stream));
+        use(h);
+        if (check_err(D)) return -1;
+        for (size_t i = chunks[k].i0; i < chunks[k].i1; ++i)
+            memcpy(static_cast<uint8_t *>(out) + (size_t)idx[i] * os.row_bytes,
+                   h.out + (i - chunks[k].i0) * os.row_bytes, os.row_bytes);
+        return 0;
+    };
+    auto enqueue = [&](size_t k) -> int {
+        const Chunk &ch = chunks[k];
+        use(sets[k & 1]);
         int off = 0;
-        for (int b = 0; b < B; ++b) {
-            const ffwd_input_t &in = inputs[idx[i0 + b]];
+        for (int b = 0; b < ch.B; ++b) {
+            const ffwd_input_t &in = inputs[idx[ch.i0 + b]];
             w.h_offsets[b] = off;
             for (int t = 0; t < in.n_tokens; ++t) {
                 const int id = in.ids[t];
                 if (id < 0 || id >= c.vocab_size) {
-                    fail("invalid token id %d at input %d position %d", id, idx[i0 + b], t);
+                    fail("invalid token id %d at input %d position %d", id, idx[ch.i0 + b], t);
                     return -1;
                 }
             }
             memcpy(w.h_ids + off, in.ids, (size_t)in.n_tokens * 4);
             off += in.n_tokens;
         }
-        w.h_offsets[B] = off;
-        CK(cudaMemcpyAsync(w.ids, w.h_ids, (size_t)T * 4, cudaMemcpyHostToDevice, D.stream));
-        CK(cudaMemcpyAsync(w.offsets, w.h_offsets, (size_t)(B + 1) * 4, cudaMemcpyHostToDevice,
+        w.h_offsets[ch.B] = off;
+        CK(cudaMemcpyAsync(w.ids, w.h_ids, (size_t)ch.T * 4, cudaMemcpyHostToDevice, D.stream));
+        CK(cudaMemcpyAsync(w.offsets, w.h_offsets, (size_t)(ch.B + 1) * 4, cudaMemcpyHostToDevice,
                            D.stream));
         CK(cudaMemsetAsync(w.err, 0, 4, D.stream));
-        if (forward(ctx, D, T, B, w.h_offsets)) return -1;
-        LAUNCH(pool_launch(w.x, w.offsets, B, H, c.pooling_mode,
+        if (forward(ctx, D, ch.T, ch.B, w.h_offsets)) return -1;
+        LAUNCH(pool_launch(w.x, w.offsets, ch.B, H, c.pooling_mode,
                            c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm, c.rms_norm_eps,
                            c.normalize_embeddings, w.pooled, w.err, D.stream));
         const void *src = w.pooled;
@@ -931,22 +1020,25 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
             // The FFN activation buffer is free after the forward: T >= B rows
             // of intermediate_size bf16 values, at least the 4 * H bytes of an
             // f32 row (intermediate_size >= 2 * hidden in every supported model).
-            LAUNCH(encode_rows_launch(w.pooled, B, H, os.dims, os.renorm, os.enc, w.hmid, w.err,
-                                      D.stream));
+            LAUNCH(encode_rows_launch(w.pooled, ch.B, H, os.dims, os.renorm, os.enc, w.hmid,
+                                      w.err, D.stream));
             src = w.hmid;
         }
-        CK(cudaMemcpyAsync(w.h_out, src, (size_t)B * os.row_bytes, cudaMemcpyDeviceToHost,
+        CK(cudaMemcpyAsync(w.h_out, src, (size_t)ch.B * os.row_bytes, cudaMemcpyDeviceToHost,
                            D.stream));
         CK(cudaMemcpyAsync(w.h_err, w.err, 4, cudaMemcpyDeviceToHost, D.stream));
-        CK(cudaStreamSynchronize(D.stream));
-        if (check_err(D)) return -1;
-        for (int b = 0; b < B; ++b)
-            memcpy(static_cast<uint8_t *>(out) + (size_t)idx[i0 + b] * os.row_bytes,
-                   reinterpret_cast<const uint8_t *>(w.h_out) + (size_t)b * os.row_bytes,
-                   os.row_bytes);
-        i0 = i1;
+        if (chunks.size() > 1) CK(cudaEventRecord(D.fwd_done[k & 1], D.stream));
+        return 0;
+    };
+    int rc = 0;
+    for (size_t k = 0; rc == 0 && k < chunks.size(); ++k) {
+        rc = enqueue(k);
+        if (rc == 0 && k >= 1) rc = finish(k - 1);
     }
-    return 0;
+    if (rc == 0) rc = finish(chunks.size() - 1);
+    if (rc != 0) cudaStreamSynchronize(D.stream);  // nothing in flight reads the staging
+    use(set_a);
+    return rc;
 }
 
 double seq_cost(const ffwd_b200_ctx *ctx, int L) {

@@ -222,3 +222,27 @@ def test_output_encodings(key, mode, model_root):
     for bad in ((0, "f32"), (H + 1, "f32"), (12, "binary")):
         with pytest.raises(native.FfwdError):
             m.encode_batch_as(seqs, bad[0], True, bad[1])
+
+
+def test_pipelined_forwards_errors_and_encodings(model_root):
+    """Several forwards per call (tiny token budget): outputs in input order for
+    every output form, an invalid id in a later forward fails the call, and the
+    context stays usable."""
+    s = small_spec("qwen3-2l")
+    d = synth.ensure_model(s, model_root)
+    seqs = small_batch("qwen3-2l", n=9, max_len=150, seed=7)
+    whole = model(d, "bf16").encode_batch(seqs)
+    native.lib().ffwd_b200_set_max_tokens(200)
+    try:
+        m = native.B200Model(d, gemm_mode="bf16")
+        assert np.array_equal(m.encode_batch(seqs), whole)
+        assert np.array_equal(m.encode_batch_as(seqs, m.hidden, False, "binary"),
+                              of.binary_bits(whole))
+        bad = [q.copy() for q in seqs]
+        bad[-1][3] = s.vocab  # invalid id in the last forward
+        with pytest.raises(native.FfwdError):
+            m.encode_batch(bad)
+        assert np.array_equal(m.encode_batch(seqs), whole)
+        m.close()
+    finally:
+        native.lib().ffwd_b200_set_max_tokens(262144)
