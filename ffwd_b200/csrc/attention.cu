@@ -354,7 +354,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (!mbar_wait(&o_full[b], p_k & 1, p.err, &abort_sh)) return false;
             tc_fence_after();
             const float inv = p_l > 0.0f ? 1.0f / p_l : 0.0f;
-#pragma unroll 1
+            // Read O_b into packed bf16 registers and release it at once (the
+            // next item's first PV may start), then write the row with 32-byte
+            // stores (one full sector each).
+            uint32_t pk[D / 2];
+#pragma unroll
             for (int c = 0; c < D / C::CW; ++c) {
                 float o[C::CW];
                 if constexpr (C::CW == 32)
@@ -362,19 +366,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 else
                     tmem_ld16(tO + c * 16, o);
                 tmem_wait_ld();
-                if (p_store) {
-                    uint4 *op = reinterpret_cast<uint4 *>(p_orow + c * C::CW);
 #pragma unroll
-                    for (int u = 0; u < C::CW / 8; ++u)
-                        op[u] = make_uint4(pack_bf16x2(o[8 * u] * inv, o[8 * u + 1] * inv),
-                                           pack_bf16x2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
-                                           pack_bf16x2(o[8 * u + 4] * inv, o[8 * u + 5] * inv),
-                                           pack_bf16x2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
-                }
+                for (int i = 0; i < C::CW / 2; ++i)
+                    pk[c * (C::CW / 2) + i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&o_free[b]);
+            if (p_store) {
+#pragma unroll
+                for (int u = 0; u < D / 16; ++u)
+                    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(
+                                     p_orow + u * 16),
+                                 "r"(pk[8 * u]), "r"(pk[8 * u + 1]), "r"(pk[8 * u + 2]),
+                                 "r"(pk[8 * u + 3]), "r"(pk[8 * u + 4]), "r"(pk[8 * u + 5]),
+                                 "r"(pk[8 * u + 6]), "r"(pk[8 * u + 7])
+                                 : "memory");
+            }
             return true;
         };
         int g = 0;
