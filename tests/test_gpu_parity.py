@@ -246,3 +246,20 @@ def test_pipelined_forwards_errors_and_encodings(model_root):
         m.close()
     finally:
         native.lib().ffwd_b200_set_max_tokens(262144)
+
+
+def test_qwen3_8b_shape_long_documents(model_root):
+    """BASELINE config 5 shapes (hidden 4096, 32 / 8 heads x 128, SwiGLU 12288,
+    8192-token documents, last-token pooling, Matryoshka truncation to 1024 then
+    L2), one layer and a small vocabulary so the checker runs in seconds."""
+    s = synth.spec("qwen3-8b", n_layers=1, vocab=4096)
+    d = synth.ensure_model(s, model_root)
+    rng = np.random.default_rng(31)
+    seqs = [rng.integers(0, s.vocab - 1, size=L).astype(np.int32) for L in (8192, 1500)]
+    for q in seqs:
+        q[-1] = s.vocab - 1
+    ref = of.OracleModel(d).encode_batch(seqs)
+    m = model(d, "bf16")
+    check(m.encode_batch(seqs), ref, False)
+    trunc = m.encode_batch_as(seqs, 1024, True, "f32")
+    check(trunc, of.truncate_renormalize(ref, 1024), False)
