@@ -377,8 +377,11 @@ def run_ours(args, dist):
     e2e_local = time.perf_counter() - t0
     e2e_max = dist.max(torch, e2e_local)
     e2e_value = total_tokens * args.steps / e2e_max
-    n_items = int(sum((L + 127) // 128 for L in lens))
-    h2d = T * 4 + (B + 1) * 4 + n_items * 8
+    # attention work list: pairs of 128-row query blocks per key/value head
+    # (AttnItem, 6 ints), plus the ids and row offsets
+    rep = spec.n_heads // spec.n_kv_heads
+    n_items = int(sum((L + 127) // 128 for L in lens)) * spec.n_kv_heads * ((rep + 1) // 2)
+    h2d = T * 4 + (B + 1) * 4 + n_items * 24
     d2h = B * H * 4 + 4
 
     # p50 micro-batch latency, server packing (length-sorted, <= 32 inputs,
