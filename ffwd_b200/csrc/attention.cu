@@ -93,7 +93,7 @@ __device__ __forceinline__ ItemGeo item_geo(const AttnParams &p, int idx) {
     return g;
 }
 
-template <int D>
+template <int D, bool F16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm, const AttnParams p) {
     using C = AttnCfg<D>;
@@ -205,8 +205,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // several times that, so the barrier of the next step is probed
             // (non-blocking) before the current MMAs are issued and only
             // waited on when the probe failed.
-            constexpr uint32_t IDESC_S = idesc_f16(128, kTile, 1, 1, 0, 0);
-            constexpr uint32_t IDESC_O = idesc_f16(128, D, 1, 1, 0, 1);
+            constexpr int BF = F16 ? 0 : 1;
+            constexpr uint32_t IDESC_S = idesc_f16(128, kTile, BF, BF, 0, 0);
+            constexpr uint32_t IDESC_O = idesc_f16(128, D, BF, BF, 0, 1);
             const uint64_t dQ = smem_desc(smem_u32(sQ), 16, C::SBO, C::LAYOUT);
             const uint64_t dRingK = smem_desc(smem_u32(sRing), 16, C::SBO, C::LAYOUT);
             const uint64_t dRingV = smem_desc(smem_u32(sRing), C::BOX_BYTES, C::SBO, C::LAYOUT);
@@ -368,7 +369,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < C::CW / 2; ++i)
-                    pk[c * (C::CW / 2) + i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
+                    pk[c * (C::CW / 2) + i] = pack16x2(o[2 * i] * inv, o[2 * i + 1] * inv, F16);
             }
             tc_fence_before();
             __syncwarp();
@@ -445,7 +446,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         const float2 x = fma_f32x2(make_float2(s[e0], s[e0 + 1]), scale2, neg_m2);
                         const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
                         la[i & 1].x += pp.x; la[i & 1].y += pp.y;
-                        pk[i] = pack_bf16x2(pp.x, pp.y);
+                        pk[i] = pack16x2(pp.x, pp.y, F16);
                     }
                     tmem_st32u(tS + h * 32, pk);
                 }
@@ -598,25 +599,27 @@ int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStr
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     dim3 grid(p.n_items < sms ? p.n_items : sms);  // persistent
     cudaError_t e;
+#define ATTN_TC(DD, FF)                                                                      \
+    do {                                                                                     \
+        e = set_smem_once<attn_tc_kernel<DD, FF>>(AttnCfg<DD>::SMEM);                        \
+        if (e != cudaSuccess) return e;                                                      \
+        attn_tc_kernel<DD, FF><<<grid, kAttnThreads, AttnCfg<DD>::SMEM, stream>>>(*qkv_map, p); \
+    } while (0)
+    const bool f16 = p.f16 != 0;
     switch (p.head_dim) {
     case 32:
-        e = set_smem_once<attn_tc_kernel<32>>(AttnCfg<32>::SMEM);
-        if (e != cudaSuccess) return e;
-        attn_tc_kernel<32><<<grid, kAttnThreads, AttnCfg<32>::SMEM, stream>>>(*qkv_map, p);
+        if (f16) ATTN_TC(32, true); else ATTN_TC(32, false);
         break;
     case 64:
-        e = set_smem_once<attn_tc_kernel<64>>(AttnCfg<64>::SMEM);
-        if (e != cudaSuccess) return e;
-        attn_tc_kernel<64><<<grid, kAttnThreads, AttnCfg<64>::SMEM, stream>>>(*qkv_map, p);
+        if (f16) ATTN_TC(64, true); else ATTN_TC(64, false);
         break;
     case 128:
-        e = set_smem_once<attn_tc_kernel<128>>(AttnCfg<128>::SMEM);
-        if (e != cudaSuccess) return e;
-        attn_tc_kernel<128><<<grid, kAttnThreads, AttnCfg<128>::SMEM, stream>>>(*qkv_map, p);
+        if (f16) ATTN_TC(128, true); else ATTN_TC(128, false);
         break;
     default:
         return cudaErrorInvalidValue;
     }
+#undef ATTN_TC
     return cudaGetLastError();
 }
 

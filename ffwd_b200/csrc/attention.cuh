@@ -35,7 +35,8 @@ struct AttnParams {
     int q_col0, k_col0, v_col0;  // column of head 0 of Q / K / V inside a qkv row
     int causal;
     float scale;            // 1 / sqrt(head_dim)
-    // bf16 tensor-core path: output bf16 [T, ldo]
+    // tensor-core path: qkv and output [T, ldo] in bf16, or f16 when f16 is set
+    int f16;
     __nv_bfloat16 *out;
     int ldo;
     // f32 path
@@ -61,7 +62,7 @@ int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int 
 int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, const int *h_offsets,
                           int batch);
 
-// Tensor-core path.  `qkv_map`: 2-D bf16 map over the qkv matrix with a box of
+// Tensor-core path.  `qkv_map`: 2-D 16-bit map over the qkv matrix with a box of
 // 128 rows x min(head_dim, 64) columns (128-byte swizzle, or 64-byte for
 // head_dim 32).
 int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStream_t stream);

@@ -115,7 +115,8 @@ int make_map_dt(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, u
     return 0;
 }
 
-// 2-D bf16 row-major matrix [rows, cols]; box = box_rows x box_cols.
+// 2-D 16-bit row-major matrix [rows, cols]; box = box_rows x box_cols.  Also used
+// for f16 operands: TMA loads copy the 2-byte elements without conversion.
 int make_map(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows,
              uint32_t box_cols, CUtensorMapSwizzle sw) {
     return make_map_dt(m, ptr, rows, cols, box_rows, box_cols, sw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
@@ -131,7 +132,9 @@ int make_epi_map(CUtensorMap *m, const GemmParams &p) {
         return make_map_dt(m, p.out, p.M, p.ldo, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
     return make_map_dt(m, p.out, p.M, p.ldo, 128, 32, CU_TENSOR_MAP_SWIZZLE_64B,
-                       CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+                       p.out_mode == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                       2);
 }
 
 // ------------------------------------------------------------------ model state
@@ -228,7 +231,8 @@ struct Device {
 
 struct ffwd_b200_ctx {
     ffwd_config_t cfg;
-    int prec = 0;  // 0 bf16, 2 split 2-pass, 3 split 3-pass
+    int prec = 0;      // 0 single pass, 2 split 2-pass, 3 split 3-pass
+    bool f16 = false;  // single-pass operands in f16 (else bf16)
     std::vector<fb::Device> devs;
     float lin_flops_per_token = 0.0f;
     int token_dim = 0;  // late interaction: 1_Dense output width (0: pooled model)
@@ -270,8 +274,12 @@ struct HostMat {
 // parts: row blocks concatenated in order (e.g. Wq, Wk, Wv).  interleave > 0
 // reorders two equal parts [G; U] as G0 U0 G1 U1 ... in blocks of `interleave`
 // rows, so one BN-wide GEMM tile holds matching gate and up columns.
+// store: the device weight storage the values are first rounded to (0 f32,
+// 1 bf16, 2 f16; libffwd/cuda.cu upload_weight 262-305).  The encoding is then
+// f16 (out_f16, single-pass f16 GEMM), or bf16 hi (+ lo = bf16(v - hi) when split).
 bool prep_mat(const std::vector<const TensorView *> &parts, const std::vector<std::string> &names,
-              int cols, bool split, int interleave, HostMat &hm, std::string &err) {
+              int cols, int store, bool split, bool out_f16, int interleave, HostMat &hm,
+              std::string &err) {
     int rows = 0;
     for (size_t i = 0; i < parts.size(); ++i) {
         const TensorView *t = parts[i];
@@ -310,13 +318,23 @@ bool prep_mat(const std::vector<const TensorView *> &parts, const std::vector<st
             const size_t so = (size_t)src_row[r] * cols;
             uint16_t *dh = hm.hi.data() + (size_t)r * cols;
             uint16_t *dl = split ? hm.lo.data() + (size_t)r * cols : nullptr;
-            if (t->dtype == DType::BF16) {
+            if (t->dtype == DType::BF16 && !out_f16 && store != 2) {
+                memcpy(dh, (const uint16_t *)t->data + so, (size_t)cols * 2);
+            } else if (t->dtype == DType::F16 && out_f16) {
                 memcpy(dh, (const uint16_t *)t->data + so, (size_t)cols * 2);
             } else {
                 for (int c = 0; c < cols; ++c) {
-                    float v = t->dtype == DType::F32 ? ((const float *)t->data)[so + c]
-                                                     : f16_to_f32(((const uint16_t *)t->data)[so + c]);
-                    uint16_t h = f32_to_bf16_rne(v);
+                    const uint16_t w = ((const uint16_t *)t->data)[so + c];
+                    float v = t->dtype == DType::F32    ? ((const float *)t->data)[so + c]
+                              : t->dtype == DType::BF16 ? bf16_to_f32(w)
+                                                        : f16_to_f32(w);
+                    if (store == 1) v = bf16_to_f32(f32_to_bf16_rne(v));
+                    else if (store == 2) v = f16_to_f32(f32_to_f16_rne(v));
+                    if (out_f16) {
+                        dh[c] = f32_to_f16_rne(v);
+                        continue;
+                    }
+                    const uint16_t h = f32_to_bf16_rne(v);
                     dh[c] = h;
                     if (dl) dl[c] = f32_to_bf16_rne(v - bf16_to_f32(h));
                 }
@@ -399,6 +417,8 @@ int ensure_rope(Device &D, const ffwd_config_t &c, int n_pos) {
 struct HostModel {
     ffwd_config_t cfg;
     int prec = 0;
+    int store = 0;     // weight storage: 0 f32, 1 bf16, 2 f16
+    bool f16 = false;  // single-pass operands are f16 (else bf16)
     std::string prefix;
     SafeTensors st;
 };
@@ -421,7 +441,7 @@ int load_device(HostModel &hm, Device &D, std::string &err) {
         std::vector<const TensorView *> parts;
         for (auto &n : names) parts.push_back(T(n));
         HostMat h;
-        if (!prep_mat(parts, names, cols, split_w, interleave, h, err)) return -1;
+        if (!prep_mat(parts, names, cols, hm.store, split_w, hm.f16, interleave, h, err)) return -1;
         return upload_mat(D, h, bn, m);
     };
 
@@ -658,10 +678,13 @@ bool use_gemm2() {
     return on;
 }
 
-int gemm(Device &D, int prec, const CUtensorMap *a, const CUtensorMap *a_lo, const Mat &w,
+// f16: single-pass operands (and 16-bit outputs) are f16 rather than bf16.
+int gemm(Device &D, int prec, bool f16, const CUtensorMap *a, const CUtensorMap *a_lo, const Mat &w,
          GemmParams &p) {
     p.N = w.rows;
     p.K = w.cols;
+    p.op_f16 = f16 && prec == 0;
+    if (p.op_f16 && p.out_mode == kOutBF16) p.out_mode = kOutF16;
     const int passes = prec == 0 ? 1 : prec;
     if (passes == 1 && w.bn == 256 && p.out_mode != kOutSplit && use_gemm2()) {
         CUtensorMap mo;
@@ -743,8 +766,9 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
     ap.out_lo = w.att_lo;
     ap.err = w.err;
     ap.sched = w.err + 2;
+    ap.f16 = ctx->f16 ? 1 : 0;
 
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0};
     LAUNCH((positions_kernel<<<B, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0, w.pos),
             cudaGetLastError()));
     if (bert)
@@ -768,7 +792,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
     const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
     cudaStream_t s = D.stream;
     const LayerW &l = D.layers[li];
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0};
     switch (op) {
     case kOpQKV: {  // QKV projection (+ bias, + QK-norm and RoPE on the decoder)
         GemmParams p{};
@@ -794,7 +818,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
             p.head_dim = c.head_dim;
             p.eps = c.rms_norm_eps;
         }
-        return gemm(D, prec, &fs.m_xb, &fs.m_xb_lo, l.qkv, p);
+        return gemm(D, prec, ctx->f16, &fs.m_xb, &fs.m_xb_lo, l.qkv, p);
     }
     case kOpAttn:
         if (split)
@@ -810,7 +834,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
         p.ldr = H;
         p.bias = l.b_o;
         p.err = w.err;
-        return gemm(D, prec, &fs.m_att, &fs.m_att_lo, l.o, p);
+        return gemm(D, prec, ctx->f16, &fs.m_att, &fs.m_att_lo, l.o, p);
     }
     case kOpNorm1:
         if (bert)
@@ -833,7 +857,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
         } else {
             p.epi = kEpiSwiGLU;
         }
-        return gemm(D, prec, &fs.m_xb, &fs.m_xb_lo, l.up, p);
+        return gemm(D, prec, ctx->f16, &fs.m_xb, &fs.m_xb_lo, l.up, p);
     }
     case kOpDown: {  // FFN down + residual (+ bias)
         GemmParams p{};
@@ -843,7 +867,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
         p.ldr = H;
         p.bias = l.b_down;
         p.err = w.err;
-        return gemm(D, prec, &fs.m_h, &fs.m_h_lo, l.down, p);
+        return gemm(D, prec, ctx->f16, &fs.m_h, &fs.m_h_lo, l.down, p);
     }
     case kOpNorm2:
         if (bert)
@@ -1114,6 +1138,11 @@ FFWD_B200_API int ffwd_b200_set_weights_f16(int on) {
     return 0;
 }
 
+FFWD_B200_API int ffwd_b200_set_weights_default(void) {
+    g_weight_override = -1;
+    return 0;
+}
+
 FFWD_B200_API int ffwd_b200_set_devices(const int *devices, int n) {
     if (n <= 0 || !devices) return -1;
     g_devices.assign(devices, devices + n);
@@ -1188,9 +1217,17 @@ ffwd_b200_ctx *load_ctx(const char *model_dir) {
         return nullptr;
     }
 
-    // Precision plan (mirrors libffwd/cuda.cu:189-247, 4225-4237, 5010-5019):
-    // weight storage follows the override, else the file dtype; the decoder
-    // with 16-bit weights always runs 16-bit operands.
+    // Precision plan (mirrors libffwd/cuda.cu:189-247, 4225-4237, 5010-5019 and
+    // linear_ex 2905-2964).  Weight storage follows the override, else the
+    // file: BF16 files store bf16, F32 and F16 files f32 (the CPU model widens
+    // F16 at load, model.c:158-172, so the embedding table reads as F32).
+    //   decoder: bf16 storage -> bf16 operands; f16 storage -> activations cast
+    //     to f16, f16 operands; f32 storage -> the GEMM mode (f32 / tf32:
+    //     split-bf16 3-pass; bf16 / 16f: single-pass bf16 / f16).
+    //   BERT: f32 / tf32 widen 16-bit storage back (bf16: 2-pass over exact bf16
+    //     weights; f16 or f32: 3-pass, an f16 weight being exact as hi + lo);
+    //     bf16 / 16f run single-pass operands of the stored 16-bit type, or of
+    //     the mode's type for f32 storage.
     const std::string probe = c.family == FFWD_FAMILY_BERT
                                   ? hm->prefix + "encoder.layer.0.attention.self.query.weight"
                                   : hm->prefix + "layers.0.self_attn.q_proj.weight";
@@ -1199,19 +1236,31 @@ ffwd_b200_ctx *load_ctx(const char *model_dir) {
         fail("tensor not found: %s", probe.c_str());
         return nullptr;
     }
-    const bool w16 = g_weight_override >= 1 ||
-                     (g_weight_override < 0 && (pt->dtype == DType::BF16 || pt->dtype == DType::F16));
+    const int store = g_weight_override >= 0 ? g_weight_override : (pt->dtype == DType::BF16 ? 1 : 0);
     const bool exact = g_gemm_mode <= 1;
     int prec;
-    if (c.family != FFWD_FAMILY_BERT)
-        prec = w16 ? 0 : (exact ? 3 : 0);
-    else
-        prec = exact ? (w16 ? 2 : 3) : 0;
+    bool f16 = false;
+    if (c.family != FFWD_FAMILY_BERT) {
+        if (store == 0 && exact) {
+            prec = 3;
+        } else {
+            prec = 0;
+            f16 = store == 2 || (store == 0 && g_gemm_mode == 3);
+        }
+    } else if (exact) {
+        prec = store == 1 ? 2 : 3;
+    } else {
+        prec = 0;
+        f16 = store == 2 || (store == 0 && g_gemm_mode == 3);
+    }
     hm->prec = prec;
+    hm->store = store;
+    hm->f16 = f16;
 
     auto *ctx = new ffwd_b200_ctx();
     ctx->cfg = c;
     ctx->prec = prec;
+    ctx->f16 = f16;
     const int qkv_out = c.q_dim + 2 * c.kv_dim;
     ctx->lin_flops_per_token =
         2.0f * c.n_layers *
@@ -1260,7 +1309,9 @@ FFWD_B200_API const ffwd_config_t *ffwd_b200_config(const ffwd_b200_ctx_t *ctx) 
     return ctx ? &ctx->cfg : nullptr;
 }
 
-FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx) { return ctx ? ctx->prec : -1; }
+FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx) {
+    return ctx ? (ctx->prec == 0 && ctx->f16 ? 1 : ctx->prec) : -1;
+}
 
 FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts, int *part) {
     if (n < 0 || n_parts <= 0 || (n > 0 && (!cost || !part))) return -1;
@@ -2014,8 +2065,9 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     ap.out_lo = w.att_lo;
     ap.err = w.err;
     ap.sched = w.err + 2;
+    ap.f16 = ctx->f16 ? 1 : 0;
 
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr};
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0};
     LAUNCH((positions_kernel<<<batch, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0,
                                                    w.pos),
             cudaGetLastError()));

@@ -129,7 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------------------------------------------------- MMA issuer
-            constexpr uint32_t IDESC = idesc_f16(BM, BN, 1, 1, 0, 0);
+            const int bf = p.op_f16 ? 0 : 1;
+            const uint32_t IDESC = idesc_f16(BM, BN, bf, bf, 0, 0);
             int it = 0, lt = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++lt) {

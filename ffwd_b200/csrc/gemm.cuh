@@ -29,12 +29,14 @@ enum OutMode : int {
     kOutBF16 = 0,
     kOutF32 = 1,
     kOutSplit = 2,  // bf16 hi in `out`, bf16 lo (x - hi) in `out_lo`
+    kOutF16 = 3,
 };
 
 struct GemmParams {
     int M, N, K;
     int epi;
     int out_mode;
+    int op_f16;            // A and B are f16 (else bf16)
     void *out;
     void *out_lo;
     int ldo;               // output row stride (elements)
@@ -55,7 +57,7 @@ struct GemmParams {
     int *err;
 };
 
-// Host launcher.  Each tensor map is 2-D bf16 with a 64-column (128-byte) box
+// Host launcher.  Each tensor map is 2-D 16-bit (bf16, or f16 with op_f16) with a 64-column (128-byte) box
 // and 128-byte swizzle: A maps cover X (box rows 128), B maps cover W (box rows
 // BN).  `passes` = 1: A*B; 2: (A + A_lo)*B; 3: A*B + A*B_lo + A_lo*B.
 // Returns a cudaError_t value.

@@ -143,13 +143,14 @@ struct TmaSink {
         if (p.out_mode == kOutF32) {
             put_f32(buf, v);
         } else {
+            const bool f16 = p.out_mode == kOutF16;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
                 *reinterpret_cast<uint4 *>(buf + r * 64 + ((c ^ ((r >> 1) & 3)) * 16)) =
-                    make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]),
-                               pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
-                               pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
-                               pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+                    make_uint4(pack16x2(v[8 * c], v[8 * c + 1], f16),
+                               pack16x2(v[8 * c + 2], v[8 * c + 3], f16),
+                               pack16x2(v[8 * c + 4], v[8 * c + 5], f16),
+                               pack16x2(v[8 * c + 6], v[8 * c + 7], f16));
         }
         publish(buf, col, false);
     }
@@ -254,7 +255,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         if (leader && lane == 0) {
             // ---------------------------------------------------------- MMA issuer
-            constexpr uint32_t IDESC = idesc_f16(2 * BM, BN, 1, 1, 0, 0);
+            const int bf = p.op_f16 ? 0 : 1;
+            const uint32_t IDESC = idesc_f16(2 * BM, BN, bf, bf, 0, 0);
             int it = 0, lt = 0;
             bool ok = true;
             for (int tile = pair; ok && tile < num_tiles; tile += n_pairs, ++lt) {

@@ -46,14 +46,20 @@ __device__ __forceinline__ void store_row32(const GemmParams &p, int row, int co
     }
     uint32_t hi[16];
     uint32_t lo[16];
+    if (p.out_mode == kOutF16) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * i]);
-        __nv_bfloat16 h1 = __float2bfloat16_rn(v[2 * i + 1]);
-        __nv_bfloat162 hh(h0, h1);
-        hi[i] = *reinterpret_cast<uint32_t *>(&hh);
-        if (p.out_mode == kOutSplit)
-            lo[i] = pack_bf16x2(v[2 * i] - __bfloat162float(h0), v[2 * i + 1] - __bfloat162float(h1));
+        for (int i = 0; i < 16; ++i) hi[i] = pack_f16x2(v[2 * i], v[2 * i + 1]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * i]);
+            __nv_bfloat16 h1 = __float2bfloat16_rn(v[2 * i + 1]);
+            __nv_bfloat162 hh(h0, h1);
+            hi[i] = *reinterpret_cast<uint32_t *>(&hh);
+            if (p.out_mode == kOutSplit)
+                lo[i] = pack_bf16x2(v[2 * i] - __bfloat162float(h0),
+                                    v[2 * i + 1] - __bfloat162float(h1));
+        }
     }
     uint4 *o = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.out) + off);
 #pragma unroll

@@ -30,6 +30,31 @@ float bf16_to_f32(uint16_t b) {
     return f;
 }
 
+uint16_t f32_to_f16_rne(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    const uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+    const uint32_t a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return sign | 0x7E00u;    // NaN
+    if (a >= 0x477FF000u) return sign | 0x7C00u;   // |x| >= 65520 rounds to inf
+    uint32_t r, rem, half;
+    if (a < 0x38800000u) {                         // below 2^-14: subnormal result
+        const uint32_t e = a >> 23;
+        const uint32_t shift = 126 - e;            // value = m * 2^(e - 150); unit 2^-24
+        if (shift > 24) return sign;
+        const uint32_t m = (a & 0x7FFFFFu) | 0x800000u;
+        r = m >> shift;
+        rem = m & ((1u << shift) - 1);
+        half = 1u << (shift - 1);
+    } else {
+        r = ((((a >> 23) - 112) << 10) | ((a & 0x7FFFFFu) >> 13));
+        rem = a & 0x1FFFu;
+        half = 0x1000u;
+    }
+    if (rem > half || (rem == half && (r & 1u))) ++r;  // a carry moves into the exponent
+    return (uint16_t)(sign | r);
+}
+
 float f16_to_f32(uint16_t h) {
     uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
     uint32_t exp = (h >> 10) & 0x1F;

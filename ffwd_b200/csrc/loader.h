@@ -55,5 +55,7 @@ bool tensor_to_f32(const TensorView *t, const std::vector<int64_t> &shape, std::
 uint16_t f32_to_bf16_rne(float x);
 float bf16_to_f32(uint16_t b);
 float f16_to_f32(uint16_t h);
+// IEEE binary16, round to nearest even (subnormals kept, overflow to inf).
+uint16_t f32_to_f16_rne(float x);
 
 }  // namespace fb

@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #ifndef FFWD_B200_SPIN_PROBE
 #define FFWD_B200_SPIN_PROBE mbar_try_wait
@@ -369,6 +370,16 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_bf16, int b
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// Two values in the 16-bit operand type of the kind::f16 MMAs (RNE).
+__device__ __forceinline__ uint32_t pack16x2(float lo, float hi, bool f16) {
+    return f16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
 }
 
 // Split f32 into bf16 hi (RNE) + bf16 lo (RNE of the remainder).

@@ -47,6 +47,12 @@ __device__ __forceinline__ void load8_ro_f32(const float *p, float (&v)[8]) {
 
 __device__ __forceinline__ void store8_out(RowOut o, size_t off, const float (&v)[8]) {
     uint32_t hi[4], lo[4];
+    if (o.f16) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hi[i] = pack_f16x2(v[2 * i], v[2 * i + 1]);
+        *reinterpret_cast<uint4 *>(o.hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * i]);

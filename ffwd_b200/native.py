@@ -67,6 +67,7 @@ ABI = {
     "ffwd_b200_set_fast_gemm": (ctypes.c_int, [ctypes.c_char_p]),
     "ffwd_b200_set_weights_bf16": (ctypes.c_int, [ctypes.c_int]),
     "ffwd_b200_set_weights_f16": (ctypes.c_int, [ctypes.c_int]),
+    "ffwd_b200_set_weights_default": (ctypes.c_int, []),
     "ffwd_b200_load": (ctypes.c_void_p, [ctypes.c_char_p]),
     "ffwd_b200_free": (None, [ctypes.c_void_p]),
     "ffwd_b200_config": (ctypes.POINTER(ffwd_config_t), [ctypes.c_void_p]),
@@ -196,6 +197,8 @@ class B200Model:
                 L.ffwd_b200_set_weights_f16(1)
             elif weight_dtype == "f32":
                 L.ffwd_b200_set_weights_bf16(0)
+            elif weight_dtype == "file":
+                L.ffwd_b200_set_weights_default()
             else:
                 raise FfwdError("--gpu-weight-dtype must be f32, bf16, or f16")
         if devices is not None:

@@ -47,7 +47,7 @@ class ModelSpec:
     head_dim: int
     intermediate: int
     vocab: int
-    dtype: str                # "f32" | "bf16" (safetensors storage dtype)
+    dtype: str                # "f32" | "bf16" | "f16" (safetensors storage dtype)
     pooling: str              # "mean" | "cls" | "last"
     normalize: bool = True
     max_pos: int = 512
@@ -189,7 +189,7 @@ def _config_json(s: ModelSpec) -> dict:
             "rms_norm_eps": s.eps,
             "rope_theta": s.rope_theta,
             "max_position_embeddings": 32768,
-            "torch_dtype": "bfloat16" if s.dtype == "bf16" else "float32",
+            "torch_dtype": _TORCH_DTYPE[s.dtype],
         }
     else:
         c = {
@@ -204,11 +204,24 @@ def _config_json(s: ModelSpec) -> dict:
             "type_vocab_size": s.type_vocab,
             "hidden_act": s.hidden_act,
             "pad_token_id": s.pad_token_id,
-            "torch_dtype": "bfloat16" if s.dtype == "bf16" else "float32",
+            "torch_dtype": _TORCH_DTYPE[s.dtype],
         }
     if s.is_causal is not None:
         c["is_causal"] = bool(s.is_causal)
     return c
+
+
+_TORCH_DTYPE = {"f32": "float32", "bf16": "bfloat16", "f16": "float16"}
+_ST_DTYPE = {"f32": "F32", "bf16": "BF16", "f16": "F16"}
+
+
+def _encode(v: np.ndarray, dtype: str) -> bytes:
+    """Tensor bytes in the storage dtype (bf16 / f16 round to nearest even)."""
+    if dtype == "bf16":
+        return f32_to_bf16_bits(v).tobytes()
+    if dtype == "f16":
+        return v.astype(np.float16).tobytes()
+    return v.astype(np.float32).tobytes()
 
 
 def _safetensors_header(entries) -> bytes:
@@ -258,8 +271,8 @@ def write_model(s: ModelSpec, out_dir: str, max_shard_bytes: int = 4 << 30) -> s
     tensors = _tensor_list(s)
     # Matrices follow the storage dtype; the reference reads 1-D norms/biases
     # and BERT position/type tables as F32 or BF16 alike (load_norm_f32).
-    st_dt = "BF16" if s.dtype == "bf16" else "F32"
-    esz = 2 if s.dtype == "bf16" else 4
+    st_dt = _ST_DTYPE[s.dtype]
+    esz = 4 if s.dtype == "f32" else 2
     shards, cur, cur_bytes = [], [], 0
     for name, shape, kind in tensors:
         nb = int(np.prod(shape)) * esz
@@ -283,11 +296,7 @@ def write_model(s: ModelSpec, out_dir: str, max_shard_bytes: int = 4 << 30) -> s
             f.write(struct.pack("<Q", len(hdr)))
             f.write(hdr)
             for name, shape, kind in group:
-                v = _gen(rng, shape, kind)
-                if s.dtype == "bf16":
-                    f.write(f32_to_bf16_bits(v).tobytes())
-                else:
-                    f.write(v.astype(np.float32).tobytes())
+                f.write(_encode(_gen(rng, shape, kind), s.dtype))
     if s.late_dim > 0:
         write_late_projection(s, out_dir)
     return out_dir
@@ -304,8 +313,7 @@ def write_late_projection(s: ModelSpec, out_dir: str) -> None:
         json.dump({"in_features": s.hidden, "out_features": s.late_dim, "bias": False,
                    "activation_function": "torch.nn.modules.linear.Identity"}, f, indent=1)
     v = _gen(np.random.default_rng(s.seed + 7919), (s.late_dim, s.hidden), "w")
-    st_dt, data = ("BF16", f32_to_bf16_bits(v).tobytes()) if s.dtype == "bf16" else \
-        ("F32", v.astype(np.float32).tobytes())
+    st_dt, data = _ST_DTYPE[s.dtype], _encode(v, s.dtype)
     hdr = _safetensors_header([("linear.weight", st_dt, (s.late_dim, s.hidden), 0, len(data))])
     with open(os.path.join(dd, "model.safetensors"), "wb") as f:
         f.write(struct.pack("<Q", len(hdr)))

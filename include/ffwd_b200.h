@@ -116,15 +116,21 @@ typedef struct ffwd_b200_ctx ffwd_b200_ctx_t;
 
 /* Process-wide GEMM mode, set before any load: "f32" | "tf32" | "bf16" | "16f".
  * Replaces ffwd_cuda_set_fast_gemm (cuda.h:22; parsing at cuda.cu:169-199).
- * f32 and tf32 run split-bf16 multi-pass GEMMs and f32 attention; bf16 and 16f
- * run single-pass bf16 tensor-core GEMMs and attention. -1 on an unknown mode. */
+ * With f32 weight storage, f32 and tf32 run split-bf16 3-pass GEMMs and f32
+ * attention; bf16 runs single-pass bf16 and 16f single-pass f16 tensor-core
+ * GEMMs and attention.  16-bit weight storage: see ffwd_b200_precision.
+ * -1 on an unknown mode. */
 FFWD_B200_API int ffwd_b200_set_fast_gemm(const char *mode);
-/* Store weights as bf16 (on = 1) or in the file dtype (on = 0).
+/* Store weights as bf16 (on = 1) or as f32 (on = 0).
  * Replaces ffwd_cuda_set_weights_bf16 (cuda.h:23; cuda.cu:237-247). */
 FFWD_B200_API int ffwd_b200_set_weights_bf16(int on);
-/* Replaces ffwd_cuda_set_weights_f16 (cuda.h:24).  16-bit weights are stored as
- * bf16 on this backend. */
+/* Store weights as f16 (on = 1) or as f32 (on = 0).
+ * Replaces ffwd_cuda_set_weights_f16 (cuda.h:24; cuda.cu:243-246). */
 FFWD_B200_API int ffwd_b200_set_weights_f16(int on);
+/* Back to the default storage: BF16 files as bf16, F32 and F16 files as f32
+ * (cuda.cu:4225-4228).  No reference counterpart (its override lasts for the
+ * process). */
+FFWD_B200_API int ffwd_b200_set_weights_default(void);
 
 /* Load config + safetensors from model_dir and upload to every device of the
  * current device set.  Replaces ffwd_cuda_load (cuda.h:26; cuda.cu:4306). */
@@ -260,7 +266,8 @@ FFWD_B200_API void *ffwd_b200_stream(ffwd_b200_ctx_t *ctx, int dev);
 FFWD_B200_API long long ffwd_b200_launch_count(void);
 /* Last error message of the calling thread ("" if none). */
 FFWD_B200_API const char *ffwd_b200_last_error(void);
-/* Precision plan chosen at load: 0 = bf16, 2 = split-bf16 2-pass, 3 = 3-pass. */
+/* Precision plan chosen at load: 0 = single-pass bf16, 1 = single-pass f16,
+ * 2 = split-bf16 2-pass, 3 = split-bf16 3-pass. */
 FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx);
 
 /* Host-side LPT partition used by the sharder: assigns each of n items with

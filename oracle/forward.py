@@ -109,6 +109,8 @@ def load_tensors(model_dir: str) -> dict:
                 v = raw.view(np.float32)
             elif meta["dtype"] == "BF16":
                 v = (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+            elif meta["dtype"] == "F16":  # widened exactly at load (model.c:158-172)
+                v = raw.view(np.float16).astype(np.float32)
             else:
                 raise ValueError(meta["dtype"])
             out[name] = np.array(v, dtype=F32).reshape(meta["shape"])

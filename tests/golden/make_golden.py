@@ -9,7 +9,8 @@ cases: a query, candidate documents and kept-token lists, with the reference's
 ``ffwd_late_model_encode_tokens`` / ``_encode_docs`` vectors and
 ``ffwd_late_maxsim_batch`` scores (the steps of ``ffwd_rerank``).
 
-    python tests/golden/make_golden.py    (needs oracle/_ref, i.e. `make -C oracle`)
+    python tests/golden/make_golden.py [case ...]   (needs oracle/_ref: `make -C oracle`;
+                                                     no names: every case)
 """
 
 import dataclasses
@@ -40,6 +41,8 @@ CASES = {
     "qwen2_mean": ("qwen2-1l", lambda: small_batch("qwen2-1l", n=3, max_len=150)),
     "bert_tanh_cls": ("bert-tanh-1l", lambda: small_batch("bert-tanh-1l", n=4)),
     "qwen3_bidir": ("qwen3-bidir-1l", lambda: small_batch("qwen3-bidir-1l", n=3, max_len=140)),
+    "qwen3_f16": ("qwen3-f16-1l", lambda: small_batch("qwen3-f16-1l", n=3, max_len=200)),
+    "minilm_f16": ("minilm-f16-2l", lambda: small_batch("minilm-f16-2l", n=4)),
 }
 
 
@@ -81,9 +84,11 @@ def main_late(root):
         print(name, q_vec.shape, d_vec.shape, scores)
 
 
-def main():
+def main(only=()):
     root = tempfile.mkdtemp(prefix="ffwd_golden_")
     for name, (key, mk) in CASES.items():
+        if only and name not in only:
+            continue
         s = small_spec(key)
         d = synth.ensure_model(s, root)
         seqs = [np.asarray(q, np.int32) for q in mk()]
@@ -98,8 +103,9 @@ def main():
             expected=out.astype(np.float32),
         )
         print(name, out.shape)
-    main_late(root)
+    if not only:
+        main_late(root)
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]))

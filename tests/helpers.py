@@ -17,6 +17,9 @@ SMALL = {
     "qwen3-bidir-1l": ("qwen3-0.6b", dict(n_layers=1, vocab=4096, is_causal=False)),
     "qwen2-1l": ("qwen3-0.6b", dict(n_layers=1, vocab=4096, family="qwen2", pooling="mean")),
     "bert-tanh-1l": ("minilm", dict(n_layers=1, hidden_act="gelu_new", pooling="cls")),
+    # F16 safetensors (the reference widens them to F32 at load)
+    "qwen3-f16-1l": ("qwen3-0.6b", dict(n_layers=1, vocab=4096, dtype="f16")),
+    "minilm-f16-2l": ("minilm", dict(n_layers=2, dtype="f16")),
     # late interaction (1_Dense head)
     "qwen3-late-2l": ("qwen3-0.6b", dict(n_layers=2, vocab=8192, late_dim=128)),
     "qwen3-late-f32-1l": ("qwen3-0.6b", dict(n_layers=1, vocab=4096, dtype="f32", late_dim=6)),

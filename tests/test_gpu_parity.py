@@ -47,7 +47,7 @@ def test_golden(name, mode, model_root):
     spec, d, seqs, expected = load(name, model_root)
     m = model(d, mode)
     out = m.encode_batch(seqs)
-    exact = m.precision != 0
+    exact = m.precision >= 2
     # Decoders with bf16 weights run 16-bit regardless of the GEMM mode
     # (libffwd/cuda.cu:5010-5019); everything else follows the mode.
     if spec.family in ("qwen3", "qwen2") and spec.dtype == "bf16":
