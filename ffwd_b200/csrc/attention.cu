@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __shared__ __align__(8) uint64_t o_full[2], o_free[2];
     __shared__ __align__(8) uint64_t drain;
     __shared__ int item_sh[kItemSlots];
+    __shared__ ItemGeo geo_sh[kItemSlots];
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
@@ -151,16 +152,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             int k = 0;  // CTA-local item counter
             int q_issued = 0;
             bool ok = true;
+            // Item k + 1 is claimed when item k starts and published (index and
+            // geometry in shared memory) once item k's Q load is issued, so the
+            // claim's atomic and the work-list reads stay off the path of the
+            // roles that wait for the next item.
+            auto claim = [&](int kk) -> int {
+                const int idx = kk == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.sched, 1);
+                return idx < p.n_items ? idx : -1;
+            };
+            auto publish = [&](int kk, int idx) {
+                item_sh[kk % kItemSlots] = idx;
+                if (idx >= 0) geo_sh[kk % kItemSlots] = item_geo(p, idx);
+                mbar_arrive(&item_full[kk % kItemSlots]);
+            };
+            int idx = claim(0);
+            publish(0, idx);
             for (;; ++k) {
-                int idx = k == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(p.sched, 1);
-                if (idx >= p.n_items) idx = -1;
-                // Entry k % 4 was last read for item k - 4; every role has started
-                // item k - 3 by now (the Q wait below for item k - 1 passed), so it
-                // is free.
-                item_sh[k % kItemSlots] = idx;
-                mbar_arrive(&item_full[k % kItemSlots]);
                 if (idx < 0) break;
-                const ItemGeo g = item_geo(p, idx);
+                const int idx_next = claim(k + 1);
+                const ItemGeo g = geo_sh[k % kItemSlots];
                 const int qb = k & 1;
                 if (!mbar_wait(&q_empty[qb], ((k >> 1) & 1) ^ 1, p.err, &abort_sh)) {
                     ok = false;
@@ -172,6 +182,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         tma_load_2d(sQ + (qb * 2 + blk) * C::TILE_BYTES + bx * C::BOX_BYTES, &tm,
                                     &q_full[qb], p.q_col0 + (blk ? g.h1 : g.h0) * D + bx * C::BOXC,
                                     g.seq0 + (blk ? g.qt1 : g.qt0) * kTile);
+                // Entry (k + 1) % 4 was last read for item k - 3.  The Q wait for
+                // item k passed, so the MMA issuer has issued item k - 2's last S,
+                // which needed the P of the tile before it: every role has
+                // started item k - 3.
+                publish(k + 1, idx_next);
                 q_issued = k + 1;
                 for (int t = 0; t < 2 * g.n_kt; ++t, ++e) {
                     const int slot = e % C::RING;
@@ -188,6 +203,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                     &ring_full[slot], col + bx * C::BOXC, row);
                 }
                 if (!ok) break;
+                idx = idx_next;
             }
             if (!ok) {  // let loads in flight land before the CTA exits
                 for (int j = e - C::RING < 0 ? 0 : e - C::RING; j < e; ++j)
@@ -232,8 +248,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     ok = false;
                     return 0;
                 }
-                const int idx = item_sh[k % kItemSlots];
-                return idx < 0 ? 0 : item_geo(p, idx).n_kt;
+                return item_sh[k % kItemSlots] < 0 ? 0 : geo_sh[k % kItemSlots].n_kt;
             };
             // S_b(g) for block b of item k (Q buffer k & 1) against K(g).
             auto issue_s = [&](int b, int k, int g) {
@@ -391,9 +406,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int k = 0; ok; ++k) {
             if (!mbar_wait(&item_full[k % kItemSlots], (k / kItemSlots) & 1, p.err, &abort_sh))
                 break;
-            const int idx = item_sh[k % kItemSlots];
-            if (idx < 0) break;
-            const ItemGeo it = item_geo(p, idx);
+            if (item_sh[k % kItemSlots] < 0) break;
+            const ItemGeo it = geo_sh[k % kItemSlots];
             const int q = (b ? it.qt1 : it.qt0) * kTile + r;
             float m_used = -INFINITY, l = 0.0f;
             for (int j = 0; j < it.n_kt; ++j, ++g) {
