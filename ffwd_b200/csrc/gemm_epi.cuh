@@ -175,8 +175,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                     tmem_ld32(tbase + h0 + c * 32, v);
                     tmem_wait_ld();
                     if (p.bias && valid) add_bias32(v, p.bias, col0 + c * 32);
+                    float2 s2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = make_float2(v[2 * i], v[2 * i + 1]);
+                        s2 = fma_f32x2(x, x, s2);
+                    }
+                    ss += s2.x + s2.y;
                 }
                 inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
             }
@@ -204,18 +209,23 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                         add_bias32(x1, p.bias, col0 + c * 32);
                         add_bias32(x2, p.bias, col0 + half + c * 32);
                     }
+                    // Packed pairs: x *= w (norm weight), then the rotation with
+                    // the row's 1 / rms folded into cos and sin.
                     if (nw) {
                         const float4 *w1 = reinterpret_cast<const float4 *>(nw + c * 32);
                         const float4 *w2 = reinterpret_cast<const float4 *>(nw + half + c * 32);
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const float4 a = __ldg(w1 + i), b = __ldg(w2 + i);
-                            x1[4 * i] *= inv * a.x; x1[4 * i + 1] *= inv * a.y;
-                            x1[4 * i + 2] *= inv * a.z; x1[4 * i + 3] *= inv * a.w;
-                            x2[4 * i] *= inv * b.x; x2[4 * i + 1] *= inv * b.y;
-                            x2[4 * i + 2] *= inv * b.z; x2[4 * i + 3] *= inv * b.w;
+                            const float2 p0 = mul_f32x2(make_float2(x1[4 * i], x1[4 * i + 1]), make_float2(a.x, a.y));
+                            const float2 p1 = mul_f32x2(make_float2(x1[4 * i + 2], x1[4 * i + 3]), make_float2(a.z, a.w));
+                            const float2 q0 = mul_f32x2(make_float2(x2[4 * i], x2[4 * i + 1]), make_float2(b.x, b.y));
+                            const float2 q1 = mul_f32x2(make_float2(x2[4 * i + 2], x2[4 * i + 3]), make_float2(b.z, b.w));
+                            x1[4 * i] = p0.x; x1[4 * i + 1] = p0.y; x1[4 * i + 2] = p1.x; x1[4 * i + 3] = p1.y;
+                            x2[4 * i] = q0.x; x2[4 * i + 1] = q0.y; x2[4 * i + 2] = q1.x; x2[4 * i + 3] = q1.y;
                         }
                     }
+                    const float2 inv2 = make_float2(inv, inv), ninv2 = make_float2(-inv, -inv);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const __half2 *ch = reinterpret_cast<const __half2 *>(&cv[i]);
@@ -224,11 +234,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                         for (int u = 0; u < 4; ++u) {
                             const float2 cf = __half22float2(ch[u]), sf = __half22float2(sh[u]);
                             const int e = 8 * i + 2 * u;
-                            const float a0 = x1[e], b0 = x2[e], a1 = x1[e + 1], b1 = x2[e + 1];
-                            x1[e] = a0 * cf.x - b0 * sf.x;
-                            x2[e] = b0 * cf.x + a0 * sf.x;
-                            x1[e + 1] = a1 * cf.y - b1 * sf.y;
-                            x2[e + 1] = b1 * cf.y + a1 * sf.y;
+                            const float2 a = make_float2(x1[e], x1[e + 1]);
+                            const float2 bb = make_float2(x2[e], x2[e + 1]);
+                            const float2 ci = mul_f32x2(cf, inv2);
+                            const float2 r1 = fma_f32x2(bb, mul_f32x2(sf, ninv2), mul_f32x2(a, ci));
+                            const float2 r2 = fma_f32x2(a, mul_f32x2(sf, inv2), mul_f32x2(bb, ci));
+                            x1[e] = r1.x; x1[e + 1] = r1.y;
+                            x2[e] = r2.x; x2[e + 1] = r2.y;
                         }
                     }
                     sink.put(x1, col0 + c * 32);
