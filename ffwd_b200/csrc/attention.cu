@@ -595,6 +595,11 @@ __global__ void __launch_bounds__(kF32Threads)
     if (!qvalid) return;
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     const size_t off = (size_t)(seq0 + qi) * p.ldo + h * D + part * DS;
+    if (p.out_tf32) {
+#pragma unroll
+        for (int i = 0; i < DS; ++i) p.out_tf32[off + i] = round_tf32(acc[i] * inv);
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < DS; ++i) {
         const float v = acc[i] * inv;

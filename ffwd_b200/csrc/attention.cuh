@@ -44,6 +44,7 @@ struct AttnParams {
     int ldq;
     __nv_bfloat16 *out_hi;  // split output (hi / lo) for the next 2- or 3-pass GEMM
     __nv_bfloat16 *out_lo;
+    float *out_tf32;        // or, when set, f32 rounded to tf32 for a kind::tf32 GEMM
     int *err;
     int *sched;             // tensor-core path: 2 ints (claim counter, exit count), zero
                             // before the first launch; the kernel rewinds them on exit

@@ -231,7 +231,7 @@ struct Device {
 
 struct ffwd_b200_ctx {
     ffwd_config_t cfg;
-    int prec = 0;      // 0 single pass, 2 split 2-pass, 3 split 3-pass
+    int prec = 0;      // 0 single pass, 2 / 3 split-bf16 passes, 4 kind::tf32
     bool f16 = false;  // single-pass operands in f16 (else bf16)
     std::vector<fb::Device> devs;
     float lin_flops_per_token = 0.0f;
@@ -268,18 +268,30 @@ int upload(Device &D, T **p, const std::vector<T> &h) {
 // Host copy of one (possibly fused) projection in its device encoding.
 struct HostMat {
     std::vector<uint16_t> hi, lo;
+    std::vector<float> f32;  // tf32 plan: f32 values rounded to tf32
     int rows = 0, cols = 0;
 };
+
+// f32 rounded to the nearest tf32 value, ties away from zero (the rounding of
+// cvt.rna.tf32.f32); inf and NaN pass through.
+float round_tf32_host(float v) {
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;
+    memcpy(&v, &u, 4);
+    return v;
+}
 
 // parts: row blocks concatenated in order (e.g. Wq, Wk, Wv).  interleave > 0
 // reorders two equal parts [G; U] as G0 U0 G1 U1 ... in blocks of `interleave`
 // rows, so one BN-wide GEMM tile holds matching gate and up columns.
 // store: the device weight storage the values are first rounded to (0 f32,
 // 1 bf16, 2 f16; libffwd/cuda.cu upload_weight 262-305).  The encoding is then
-// f16 (out_f16, single-pass f16 GEMM), or bf16 hi (+ lo = bf16(v - hi) when split).
+// f16 (out_f16, single-pass f16 GEMM), tf32-rounded f32 (out_tf32, kind::tf32
+// GEMM), or bf16 hi (+ lo = bf16(v - hi) when split).
 bool prep_mat(const std::vector<const TensorView *> &parts, const std::vector<std::string> &names,
-              int cols, int store, bool split, bool out_f16, int interleave, HostMat &hm,
-              std::string &err) {
+              int cols, int store, bool split, bool out_f16, bool out_tf32, int interleave,
+              HostMat &hm, std::string &err) {
     int rows = 0;
     for (size_t i = 0; i < parts.size(); ++i) {
         const TensorView *t = parts[i];
@@ -291,7 +303,10 @@ bool prep_mat(const std::vector<const TensorView *> &parts, const std::vector<st
     }
     hm.rows = rows;
     hm.cols = cols;
-    hm.hi.resize((size_t)rows * cols);
+    if (out_tf32)
+        hm.f32.resize((size_t)rows * cols);
+    else
+        hm.hi.resize((size_t)rows * cols);
     if (split) hm.lo.assign((size_t)rows * cols, 0);
     std::vector<int> src_part(rows), src_row(rows);
     {
@@ -316,9 +331,19 @@ bool prep_mat(const std::vector<const TensorView *> &parts, const std::vector<st
         for (int r = r0; r < r1; ++r) {
             const TensorView *t = parts[src_part[r]];
             const size_t so = (size_t)src_row[r] * cols;
-            uint16_t *dh = hm.hi.data() + (size_t)r * cols;
+            uint16_t *dh = out_tf32 ? nullptr : hm.hi.data() + (size_t)r * cols;
             uint16_t *dl = split ? hm.lo.data() + (size_t)r * cols : nullptr;
-            if (t->dtype == DType::BF16 && !out_f16 && store != 2) {
+            if (out_tf32) {
+                for (int c = 0; c < cols; ++c) {
+                    const uint16_t w = ((const uint16_t *)t->data)[so + c];
+                    float v = t->dtype == DType::F32    ? ((const float *)t->data)[so + c]
+                              : t->dtype == DType::BF16 ? bf16_to_f32(w)
+                                                        : f16_to_f32(w);
+                    if (store == 1) v = bf16_to_f32(f32_to_bf16_rne(v));
+                    else if (store == 2) v = f16_to_f32(f32_to_f16_rne(v));
+                    hm.f32[(size_t)r * cols + c] = round_tf32_host(v);
+                }
+            } else if (t->dtype == DType::BF16 && !out_f16 && store != 2) {
                 memcpy(dh, (const uint16_t *)t->data + so, (size_t)cols * 2);
             } else if (t->dtype == DType::F16 && out_f16) {
                 memcpy(dh, (const uint16_t *)t->data + so, (size_t)cols * 2);
@@ -356,6 +381,14 @@ int upload_mat(Device &D, const HostMat &hm, int bn, Mat &m) {
     m.rows = hm.rows;
     m.cols = hm.cols;
     m.bn = bn;
+    if (!hm.f32.empty()) {  // tf32 plan: f32 weights, 32-column (128-byte) boxes
+        float *d = nullptr;
+        if (dev_alloc(D, &d, hm.f32.size())) return -1;
+        CK(cudaMemcpy(d, hm.f32.data(), hm.f32.size() * 4, cudaMemcpyHostToDevice));
+        m.hi = reinterpret_cast<__nv_bfloat16 *>(d);
+        return make_map_dt(&m.map_hi, d, m.rows, m.cols, bn, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
+    }
     if (dev_alloc(D, &m.hi, hm.hi.size())) return -1;
     CK(cudaMemcpy(m.hi, hm.hi.data(), hm.hi.size() * 2, cudaMemcpyHostToDevice));
     if (make_map(&m.map_hi, m.hi, m.rows, m.cols, bn, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
@@ -441,7 +474,9 @@ int load_device(HostModel &hm, Device &D, std::string &err) {
         std::vector<const TensorView *> parts;
         for (auto &n : names) parts.push_back(T(n));
         HostMat h;
-        if (!prep_mat(parts, names, cols, hm.store, split_w, hm.f16, interleave, h, err)) return -1;
+        if (!prep_mat(parts, names, cols, hm.store, split_w, hm.f16, hm.prec == 4, interleave, h,
+                      err))
+            return -1;
         return upload_mat(D, h, bn, m);
     };
 
@@ -580,7 +615,9 @@ void free_device(Device &D) {
 int ensure_ws(ffwd_b200_ctx *ctx, Device &D, int T, int B, int n_items, int n_spans) {
     Workspace &w = D.ws;
     const ffwd_config_t &c = ctx->cfg;
-    const bool split = ctx->prec != 0;
+    const bool exact = ctx->prec != 0;  // f32 qkv and attention
+    const bool split = ctx->prec == 2 || ctx->prec == 3;
+    const size_t ob = ctx->prec == 4 ? 4 : 2;  // bytes per GEMM operand element
     if (T > w.cap_t) {
         CK(cudaStreamSynchronize(D.stream));
         const int cap = std::max(T, std::min(g_max_tokens, std::max(T, 2 * w.cap_t)));
@@ -599,10 +636,10 @@ int ensure_ws(ffwd_b200_ctx *ctx, Device &D, int T, int B, int n_items, int n_sp
         CK(cudaMalloc(&w.ids, t * 4));
         CK(cudaMalloc(&w.pos, t * 4));
         CK(cudaMalloc(&w.x, t * H * 4));
-        CK(cudaMalloc(&w.xb, t * H * 2));
-        CK(cudaMalloc(&w.qkv, t * qkv * (split ? 4 : 2)));
-        CK(cudaMalloc(&w.att, t * c.q_dim * 2));
-        CK(cudaMalloc(&w.hmid, t * inter * 2));
+        CK(cudaMalloc(&w.xb, t * H * ob));
+        CK(cudaMalloc(&w.qkv, t * qkv * (exact ? 4 : 2)));
+        CK(cudaMalloc(&w.att, t * c.q_dim * ob));
+        CK(cudaMalloc(&w.hmid, t * inter * ob));
         if (split) {
             CK(cudaMalloc(&w.xb_lo, t * H * 2));
             CK(cudaMalloc(&w.att_lo, t * c.q_dim * 2));
@@ -685,16 +722,51 @@ int gemm(Device &D, int prec, bool f16, const CUtensorMap *a, const CUtensorMap 
     p.K = w.cols;
     p.op_f16 = f16 && prec == 0;
     if (p.op_f16 && p.out_mode == kOutBF16) p.out_mode = kOutF16;
-    const int passes = prec == 0 ? 1 : prec;
+    const int passes = prec == 0 ? 1 : prec;  // 4: one kind::tf32 pass
     if (passes == 1 && w.bn == 256 && p.out_mode != kOutSplit && use_gemm2()) {
         CUtensorMap mo;
         if (make_epi_map(&mo, p)) return -1;
         LAUNCH(gemm2_launch(a, &w.map_half, &mo, p, D.num_sms, D.stream));
         return 0;
     }
-    LAUNCH(gemm_launch(a, passes >= 2 ? a_lo : nullptr, &w.map_hi, passes == 3 ? &w.map_lo : nullptr,
+    LAUNCH(gemm_launch(a, passes == 2 || passes == 3 ? a_lo : nullptr, &w.map_hi,
+                       passes == 3 ? &w.map_lo : nullptr,
                        w.bn, passes, p, D.num_sms, D.stream));
     return 0;
+}
+
+// Tensor maps over the GEMM operands of one forward (and, on the 16-bit plans,
+// the qkv matrix for the tensor-core attention): 16-bit with 64-column boxes,
+// split-bf16 hi + lo, or tf32-rounded f32 with 32-column boxes.
+int make_act_maps(const ffwd_b200_ctx *ctx, FwdState &fs, const Workspace &w, int T) {
+    const ffwd_config_t &c = ctx->cfg;
+    const int H = c.hidden_size, I = c.intermediate_size, qkv_dim = c.q_dim + 2 * c.kv_dim;
+    if (ctx->prec == 4) {
+        auto m32 = [&](CUtensorMap *m, const void *ptr, int cols) {
+            return make_map_dt(m, ptr, T, cols, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
+        };
+        return m32(&fs.m_xb, w.xb, H) || m32(&fs.m_att, w.att, c.q_dim) || m32(&fs.m_h, w.hmid, I)
+                   ? -1
+                   : 0;
+    }
+    if (make_map(&fs.m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&fs.m_att, w.att, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        make_map(&fs.m_h, w.hmid, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    if (ctx->prec != 0)
+        return make_map(&fs.m_xb_lo, w.xb_lo, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                       make_map(&fs.m_att_lo, w.att_lo, T, c.q_dim, 128, 64,
+                                CU_TENSOR_MAP_SWIZZLE_128B) ||
+                       make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)
+                   ? -1
+                   : 0;
+    const CUtensorMapSwizzle sw =
+        c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    return make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64), sw) ||
+                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, std::min(c.head_dim, 64), sw)
+               ? -1
+               : 0;
 }
 
 // Upload-independent preparation: RoPE cache, attention items, tensor maps,
@@ -703,8 +775,9 @@ int gemm(Device &D, int prec, bool f16, const CUtensorMap *a, const CUtensorMap 
 int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int *h_offsets) {
     const ffwd_config_t &c = ctx->cfg;
     Workspace &w = D.ws;
-    const bool split = ctx->prec != 0;
-    const int H = c.hidden_size, I = c.intermediate_size;
+    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
+    const bool split = ctx->prec == 2 || ctx->prec == 3;
+    const int H = c.hidden_size;
     const int qkv_dim = c.q_dim + 2 * c.kv_dim;
     const bool bert = c.family == FFWD_FAMILY_BERT;
     const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
@@ -718,9 +791,9 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
 
     // Attention work list, heaviest first.
     {
-        const int n = attention_count_items(!split, c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B);
+        const int n = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B);
         if (n < 0 || ensure_ws(ctx, D, T, B, n, 0)) return -1;
-        fs.n_items = attention_build_items(!split, c.attention_mode == FFWD_ATTENTION_CAUSAL,
+        fs.n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
                                            c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B,
                                            w.h_items, w.cap_items);
         if (fs.n_items < 0) {
@@ -731,19 +804,7 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
                            cudaMemcpyHostToDevice, s));
     }
 
-    if (make_map(&fs.m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        make_map(&fs.m_att, w.att, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        make_map(&fs.m_h, w.hmid, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
-        return -1;
-    if (split && (make_map(&fs.m_xb_lo, w.xb_lo, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-                  make_map(&fs.m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-                  make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
-        return -1;
-    if (!split && (make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
-                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ||
-                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, std::min(c.head_dim, 64),
-                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
-        return -1;
+    if (make_act_maps(ctx, fs, w, T)) return -1;
 
     AttnParams &ap = fs.ap;
     ap = AttnParams{};
@@ -767,8 +828,10 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
     ap.err = w.err;
     ap.sched = w.err + 2;
     ap.f16 = ctx->f16 ? 1 : 0;
+    ap.out_tf32 = ctx->prec == 4 ? reinterpret_cast<float *>(w.att) : nullptr;
 
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0};
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0,
+                        ctx->prec == 4 ? reinterpret_cast<float *>(w.xb) : nullptr};
     LAUNCH((positions_kernel<<<B, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0, w.pos),
             cudaGetLastError()));
     if (bert)
@@ -785,21 +848,23 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
     const ffwd_config_t &c = ctx->cfg;
     Workspace &w = D.active_ws ? *D.active_ws : D.ws;
     const int prec = ctx->prec;
-    const bool split = prec != 0;
+    const bool exact = prec != 0;  // f32 qkv and CUDA-core attention
+    const bool split = prec == 2 || prec == 3;
     const int H = c.hidden_size, I = c.intermediate_size, T = fs.T;
     const int qkv_dim = c.q_dim + 2 * c.kv_dim;
     const bool bert = c.family == FFWD_FAMILY_BERT;
     const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
     cudaStream_t s = D.stream;
     const LayerW &l = D.layers[li];
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0};
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0,
+                        ctx->prec == 4 ? reinterpret_cast<float *>(w.xb) : nullptr};
     switch (op) {
     case kOpQKV: {  // QKV projection (+ bias, + QK-norm and RoPE on the decoder)
         GemmParams p{};
         p.M = T;
         p.out = w.qkv;
         p.ldo = qkv_dim;
-        p.out_mode = split ? kOutF32 : kOutBF16;
+        p.out_mode = exact ? kOutF32 : kOutBF16;
         p.bias = l.b_qkv;
         p.err = w.err;
         if (bert) {
@@ -821,7 +886,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
         return gemm(D, prec, ctx->f16, &fs.m_xb, &fs.m_xb_lo, l.qkv, p);
     }
     case kOpAttn:
-        if (split)
+        if (exact)
             LAUNCH(attention_f32_launch(fs.ap, s));
         else
             LAUNCH(attention_tc_launch(&fs.m_qkv, fs.ap, s));
@@ -848,7 +913,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
         p.out = w.hmid;
         p.out_lo = w.hmid_lo;
         p.ldo = I;
-        p.out_mode = split ? kOutSplit : kOutBF16;
+        p.out_mode = split ? kOutSplit : prec == 4 ? kOutTF32 : kOutBF16;
         p.err = w.err;
         if (bert) {
             p.epi = kEpiGelu;
@@ -939,7 +1004,7 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
                   const std::vector<int> &idx, void *out, const OutSpec &os) {
     const ffwd_config_t &c = ctx->cfg;
     const int H = c.hidden_size;
-    const bool split = ctx->prec != 0;
+    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
     CK(cudaSetDevice(D.dev));
     // Forwards of at most g_max_tokens rows, sized evenly: with n forwards
     // needed, each aims at total / n tokens, so no small tail forward runs
@@ -966,7 +1031,7 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
         const int B = (int)(i1 - i0), T = (int)tok;
         offs.assign(1, 0);
         for (size_t i = i0; i < i1; ++i) offs.push_back(offs.back() + inputs[idx[i]].n_tokens);
-        const int n_items = attention_count_items(!split, c.n_heads, c.n_kv_heads, c.head_dim,
+        const int n_items = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim,
                                                   offs.data(), B);
         if (n_items < 0) {
             fail("attention work list too large");
@@ -1222,12 +1287,13 @@ ffwd_b200_ctx *load_ctx(const char *model_dir) {
     // file: BF16 files store bf16, F32 and F16 files f32 (the CPU model widens
     // F16 at load, model.c:158-172, so the embedding table reads as F32).
     //   decoder: bf16 storage -> bf16 operands; f16 storage -> activations cast
-    //     to f16, f16 operands; f32 storage -> the GEMM mode (f32 / tf32:
-    //     split-bf16 3-pass; bf16 / 16f: single-pass bf16 / f16).
-    //   BERT: f32 / tf32 widen 16-bit storage back (bf16: 2-pass over exact bf16
+    //     to f16, f16 operands; f32 storage -> the GEMM mode (f32: split-bf16
+    //     3-pass; tf32: one kind::tf32 pass; bf16 / 16f: single-pass bf16 / f16).
+    //   BERT: f32 widens 16-bit storage back (bf16: 2-pass over exact bf16
     //     weights; f16 or f32: 3-pass, an f16 weight being exact as hi + lo);
-    //     bf16 / 16f run single-pass operands of the stored 16-bit type, or of
-    //     the mode's type for f32 storage.
+    //     tf32 runs kind::tf32 over any storage (bf16 and f16 values are exact
+    //     in tf32); bf16 / 16f run single-pass operands of the stored 16-bit
+    //     type, or of the mode's type for f32 storage.
     const std::string probe = c.family == FFWD_FAMILY_BERT
                                   ? hm->prefix + "encoder.layer.0.attention.self.query.weight"
                                   : hm->prefix + "layers.0.self_attn.q_proj.weight";
@@ -1240,13 +1306,16 @@ ffwd_b200_ctx *load_ctx(const char *model_dir) {
     const bool exact = g_gemm_mode <= 1;
     int prec;
     bool f16 = false;
+    const bool tf32 = g_gemm_mode == 1;
     if (c.family != FFWD_FAMILY_BERT) {
         if (store == 0 && exact) {
-            prec = 3;
+            prec = tf32 ? 4 : 3;
         } else {
             prec = 0;
             f16 = store == 2 || (store == 0 && g_gemm_mode == 3);
         }
+    } else if (tf32) {
+        prec = 4;
     } else if (exact) {
         prec = store == 1 ? 2 : 3;
     } else {
@@ -1594,6 +1663,36 @@ FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const voi
         LAUNCH(gemm_launch(&ma, x_lo ? &mal : nullptr, &mb, w_lo ? &mbl : nullptr, bn, passes, p,
                            sms, 0));
     }
+    CK(cudaDeviceSynchronize());
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_gemm_tf32(const float *x, const float *w, float *y, int M, int N, int K,
+                                      int bn) {
+    t_err.clear();
+    if (!x || !w || !y || M <= 0 || N <= 0 || K <= 0 || K % 64 || (bn != 128 && bn != 256) ||
+        N % bn) {
+        fail("invalid arguments");
+        return -1;
+    }
+    int dev = 0, sms = 148;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CUtensorMap ma, mb;
+    if (make_map_dt(&ma, x, M, K, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4) ||
+        make_map_dt(&mb, w, N, K, bn, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4))
+        return -1;
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.epi = kEpiStore;
+    p.out_mode = kOutF32;
+    p.out = y;
+    p.ldo = N;
+    LAUNCH(gemm_launch(&ma, nullptr, &mb, nullptr, bn, 4, p, sms, 0));
     CK(cudaDeviceSynchronize());
     return 0;
 }
@@ -1980,9 +2079,10 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     }
 
     // Attention work list, heaviest first (same builder as prepare()).
-    const bool split = ctx->prec != 0;
+    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
+    const bool split = ctx->prec == 2 || ctx->prec == 3;
     AttnItem items[kNoAllocMaxItems];
-    const int n_items = attention_build_items(!split, c.attention_mode == FFWD_ATTENTION_CAUSAL,
+    const int n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
                                               c.n_heads, c.n_kv_heads, c.head_dim, h_offsets,
                                               batch, items, kNoAllocMaxItems);
     if (n_items < 0) {
@@ -1996,14 +2096,15 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     const int H = c.hidden_size, I = c.intermediate_size, qkv_dim = c.q_dim + 2 * c.kv_dim;
     Workspace w{};
     Carver cv{base, 0, kNoAllocScratchBytes};
+    const size_t ob16 = ctx->prec == 4 ? 2 : 1;  // 16-bit units per GEMM operand element
     bool ok = cv.take(&w.err, 4) && cv.take(&w.offsets, (size_t)batch + 1) &&
               cv.take(&w.items, (size_t)n_items) && cv.take(&w.ids, (size_t)T) &&
               cv.take(&w.pos, (size_t)T) && cv.take(&w.x, (size_t)T * H) &&
-              cv.take(&w.xb, (size_t)T * H) && cv.take(&w.att, (size_t)T * c.q_dim) &&
-              cv.take(&w.hmid, (size_t)T * I);
+              cv.take(&w.xb, (size_t)T * H * ob16) && cv.take(&w.att, (size_t)T * c.q_dim * ob16) &&
+              cv.take(&w.hmid, (size_t)T * I * ob16);
     if (ok) {
         uint8_t *q = nullptr;
-        ok = cv.take(&q, (size_t)T * qkv_dim * (split ? 4 : 2));
+        ok = cv.take(&q, (size_t)T * qkv_dim * (exact ? 4 : 2));
         w.qkv = q;
     }
     if (ok && split)
@@ -2032,19 +2133,7 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     fs.n_items = n_items;
     const bool bert = c.family == FFWD_FAMILY_BERT;
     const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
-    if (make_map(&fs.m_xb, w.xb, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        make_map(&fs.m_att, w.att, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        make_map(&fs.m_h, w.hmid, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B))
-        return -1;
-    if (split && (make_map(&fs.m_xb_lo, w.xb_lo, T, H, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-                  make_map(&fs.m_att_lo, w.att_lo, T, c.q_dim, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-                  make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
-        return -1;
-    if (!split && (make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64),
-                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ||
-                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, std::min(c.head_dim, 64),
-                            c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
-        return -1;
+    if (make_act_maps(ctx, fs, w, T)) return -1;
     AttnParams &ap = fs.ap;
     ap.offsets = w.offsets;
     ap.items = w.items;
@@ -2066,8 +2155,10 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     ap.err = w.err;
     ap.sched = w.err + 2;
     ap.f16 = ctx->f16 ? 1 : 0;
+    ap.out_tf32 = ctx->prec == 4 ? reinterpret_cast<float *>(w.att) : nullptr;
 
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0};
+    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0,
+                        ctx->prec == 4 ? reinterpret_cast<float *>(w.xb) : nullptr};
     LAUNCH((positions_kernel<<<batch, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0,
                                                    w.pos),
             cudaGetLastError()));

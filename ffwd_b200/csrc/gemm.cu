@@ -27,11 +27,15 @@ using epi::kEpiGroups;
 using epi::epilogue_tile;
 constexpr int kThreads = 64 + 128 * kEpiGroups;
 
+// PASSES 1-3: bf16 / f16 operands, 64 elements per 128-byte row; PASSES 4:
+// tf32 (f32 operands), 32 elements per row.  Both take 4 MMAs of 32 bytes of K
+// per stage.
 template <int BN, int PASSES>
 struct GemmCfg {
+    static constexpr int KE = PASSES == 4 ? 32 : BK;  // K elements per stage
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
-    static constexpr int N_A = PASSES >= 2 ? 2 : 1;
+    static constexpr int N_A = PASSES == 2 || PASSES == 3 ? 2 : 1;
     static constexpr int N_B = PASSES == 3 ? 2 : 1;
     static constexpr int STAGE_BYTES = A_BYTES * N_A + B_BYTES * N_B;
     static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
@@ -63,7 +67,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int m_blocks = (p.M + BM - 1) / BM;
     const int n_blocks = p.N / BN;
     const int num_tiles = m_blocks * n_blocks;
-    const int k_blocks = p.K / BK;
+    const int k_blocks = p.K / C::KE;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -81,7 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
-        if (PASSES >= 2) tma_prefetch_desc(&tmA2);
+        if (PASSES == 2 || PASSES == 3) tma_prefetch_desc(&tmA2);
         if (PASSES == 3) tma_prefetch_desc(&tmB2);
     }
     if (warp == 1) {
@@ -110,12 +114,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t *st = smem + s * C::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
-                    tma_load_2d(st, &tmA, &full_bar[s], kb * BK, mb * BM);
-                    if (PASSES >= 2) tma_load_2d(st + C::A_BYTES, &tmA2, &full_bar[s], kb * BK, mb * BM);
+                    tma_load_2d(st, &tmA, &full_bar[s], kb * C::KE, mb * BM);
+                    if (C::N_A == 2)
+                        tma_load_2d(st + C::A_BYTES, &tmA2, &full_bar[s], kb * C::KE, mb * BM);
                     uint8_t *sb = st + C::A_BYTES * C::N_A;
-                    tma_load_2d_hint(sb, &tmB, &full_bar[s], kb * BK, nb * BN, pol_w);
+                    tma_load_2d_hint(sb, &tmB, &full_bar[s], kb * C::KE, nb * BN, pol_w);
                     if (PASSES == 3)
-                        tma_load_2d_hint(sb + C::B_BYTES, &tmB2, &full_bar[s], kb * BK, nb * BN, pol_w);
+                        tma_load_2d_hint(sb + C::B_BYTES, &tmB2, &full_bar[s], kb * C::KE, nb * BN, pol_w);
                     ++it;
                 }
             }
@@ -130,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // ---------------------------------------------------------- MMA issuer
             const int bf = p.op_f16 ? 0 : 1;
-            const uint32_t IDESC = idesc_f16(BM, BN, bf, bf, 0, 0);
+            const uint32_t IDESC = PASSES == 4 ? idesc_tf32(BM, BN) : idesc_f16(BM, BN, bf, bf, 0, 0);
             int it = 0, lt = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++lt) {
@@ -158,6 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t ad = smem_desc(sa + kk * 32, 16, 1024, kLayoutSW128);
                         const uint64_t bd = smem_desc(sb + kk * 32, 16, 1024, kLayoutSW128);
+                        if (PASSES == 4) {
+                            umma_tf32(d, ad, bd, IDESC, (kb | kk) != 0);
+                            continue;
+                        }
                         umma_f16(d, ad, bd, IDESC, (kb | kk) != 0);
                         if (PASSES >= 2) {
                             const uint64_t a2d = smem_desc(sa2 + kk * 32, 16, 1024, kLayoutSW128);
@@ -243,7 +252,7 @@ int gemm_launch(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap
                 const CUtensorMap *b_lo, int bn, int passes, const GemmParams &p, int num_sms,
                 cudaStream_t stream) {
     if (p.M <= 0 || p.K % BK != 0 || p.N % bn != 0) return cudaErrorInvalidValue;
-    if (passes >= 2 && !a_lo) return cudaErrorInvalidValue;
+    if ((passes == 2 || passes == 3) && !a_lo) return cudaErrorInvalidValue;
     if (passes == 3 && !b_lo) return cudaErrorInvalidValue;
     if (p.epi == kEpiQKRope && (p.head_dim % 64 != 0 || bn % p.head_dim != 0))
         return cudaErrorInvalidValue;
@@ -251,10 +260,12 @@ int gemm_launch(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap
         if (passes == 1) return launch_epi<256, 1>(a, a_lo, b, b_lo, p, num_sms, stream);
         if (passes == 2) return launch_epi<256, 2>(a, a_lo, b, b_lo, p, num_sms, stream);
         if (passes == 3) return launch_epi<256, 3>(a, a_lo, b, b_lo, p, num_sms, stream);
+        if (passes == 4) return launch_epi<256, 4>(a, a_lo, b, b_lo, p, num_sms, stream);
     } else if (bn == 128) {
         if (passes == 1) return launch_epi<128, 1>(a, a_lo, b, b_lo, p, num_sms, stream);
         if (passes == 2) return launch_epi<128, 2>(a, a_lo, b, b_lo, p, num_sms, stream);
         if (passes == 3) return launch_epi<128, 3>(a, a_lo, b, b_lo, p, num_sms, stream);
+        if (passes == 4) return launch_epi<128, 4>(a, a_lo, b, b_lo, p, num_sms, stream);
     }
     return cudaErrorInvalidValue;
 }

@@ -30,6 +30,7 @@ enum OutMode : int {
     kOutF32 = 1,
     kOutSplit = 2,  // bf16 hi in `out`, bf16 lo (x - hi) in `out_lo`
     kOutF16 = 3,
+    kOutTF32 = 4,   // f32 rounded to tf32 (operand of the next kind::tf32 GEMM)
 };
 
 struct GemmParams {
@@ -57,9 +58,11 @@ struct GemmParams {
     int *err;
 };
 
-// Host launcher.  Each tensor map is 2-D 16-bit (bf16, or f16 with op_f16) with a 64-column (128-byte) box
-// and 128-byte swizzle: A maps cover X (box rows 128), B maps cover W (box rows
-// BN).  `passes` = 1: A*B; 2: (A + A_lo)*B; 3: A*B + A*B_lo + A_lo*B.
+// Host launcher.  Each tensor map is 2-D with a 128-byte box row and 128-byte
+// swizzle: 16-bit (bf16, or f16 with op_f16) with 64-column boxes, or, for
+// passes = 4, f32 with 32-column boxes.  A maps cover X (box rows 128), B maps
+// cover W (box rows BN).  `passes` = 1: A*B; 2: (A + A_lo)*B;
+// 3: A*B + A*B_lo + A_lo*B; 4: A*B in kind::tf32.
 // Returns a cudaError_t value.
 int gemm_launch(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap *b,
                 const CUtensorMap *b_lo, int bn, int passes, const GemmParams &p, int num_sms,

@@ -44,6 +44,14 @@ __device__ __forceinline__ void store_row32(const GemmParams &p, int row, int co
             o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
         return;
     }
+    if (p.out_mode == kOutTF32) {
+        float4 *o = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            o[i] = make_float4(round_tf32(v[4 * i]), round_tf32(v[4 * i + 1]),
+                               round_tf32(v[4 * i + 2]), round_tf32(v[4 * i + 3]));
+        return;
+    }
     uint32_t hi[16];
     uint32_t lo[16];
     if (p.out_mode == kOutF16) {

@@ -199,6 +199,18 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::tf32 (f32 operands read as
+// tf32, K = 8 per instruction, f32 accumulate).
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16.  A (M x 16) sits in TMEM:
 // lane = row, two 16-bit elements per 32-bit column.
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
@@ -375,7 +387,20 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_bf16, int b
            | ((uint32_t)(M >> 4) << 24);  // M / 16
 }
 
+// Instruction descriptor, kind::tf32 (both operands tf32, K-major), f32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
 // ----------------------------------------------------------------- misc
+
+// f32 rounded to the nearest tf32 value (ties away from zero), as an f32.
+__device__ __forceinline__ float round_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

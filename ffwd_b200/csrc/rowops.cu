@@ -47,6 +47,12 @@ __device__ __forceinline__ void load8_ro_f32(const float *p, float (&v)[8]) {
 
 __device__ __forceinline__ void store8_out(RowOut o, size_t off, const float (&v)[8]) {
     uint32_t hi[4], lo[4];
+    if (o.tf32) {
+        float4 *d = reinterpret_cast<float4 *>(o.tf32 + off);
+        d[0] = make_float4(round_tf32(v[0]), round_tf32(v[1]), round_tf32(v[2]), round_tf32(v[3]));
+        d[1] = make_float4(round_tf32(v[4]), round_tf32(v[5]), round_tf32(v[6]), round_tf32(v[7]));
+        return;
+    }
     if (o.f16) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) hi[i] = pack_f16x2(v[2 * i], v[2 * i + 1]);

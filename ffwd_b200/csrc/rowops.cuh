@@ -19,6 +19,7 @@ struct RowOut {
     __nv_bfloat16 *hi;  // bf16 value (RNE), or f16 when f16 is set
     __nv_bfloat16 *lo;  // remainder (x - hi) in bf16, or null (single-pass GEMMs)
     int f16;            // single-pass f16 operand (lo unused)
+    float *tf32;        // when set: f32 rounded to tf32 instead (hi, lo unused)
 };
 
 // Qwen: x[t] = E[ids[t]] (f32 or bf16 table), xn = RMSNorm(x) * w (if w).

@@ -97,6 +97,8 @@ ABI = {
     "ffwd_b200_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                            ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "ffwd_b200_gemm_tf32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "ffwd_b200_encode_batch_as": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                  ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  ctypes.c_void_p]),
@@ -385,6 +387,12 @@ def lpt_partition(costs, n_parts: int) -> np.ndarray:
 
 def gemm_bf16(x_ptr, w_ptr, y_ptr, M, N, K, bn=256, x_lo_ptr=None, w_lo_ptr=None):
     rc = lib().ffwd_b200_gemm_bf16(x_ptr, x_lo_ptr, w_ptr, w_lo_ptr, y_ptr, M, N, K, bn)
+    if rc != 0:
+        raise FfwdError(f"gemm failed: {last_error()}")
+
+
+def gemm_tf32(x_ptr, w_ptr, y_ptr, M, N, K, bn=256):
+    rc = lib().ffwd_b200_gemm_tf32(x_ptr, w_ptr, y_ptr, M, N, K, bn)
     if rc != 0:
         raise FfwdError(f"gemm failed: {last_error()}")
 

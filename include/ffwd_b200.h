@@ -116,9 +116,10 @@ typedef struct ffwd_b200_ctx ffwd_b200_ctx_t;
 
 /* Process-wide GEMM mode, set before any load: "f32" | "tf32" | "bf16" | "16f".
  * Replaces ffwd_cuda_set_fast_gemm (cuda.h:22; parsing at cuda.cu:169-199).
- * With f32 weight storage, f32 and tf32 run split-bf16 3-pass GEMMs and f32
- * attention; bf16 runs single-pass bf16 and 16f single-pass f16 tensor-core
- * GEMMs and attention.  16-bit weight storage: see ffwd_b200_precision.
+ * With f32 weight storage, f32 runs split-bf16 3-pass GEMMs, tf32 kind::tf32
+ * GEMMs (both with f32 attention); bf16 runs single-pass bf16 and 16f
+ * single-pass f16 tensor-core GEMMs and attention.  16-bit weight storage: see
+ * ffwd_b200_precision.
  * -1 on an unknown mode. */
 FFWD_B200_API int ffwd_b200_set_fast_gemm(const char *mode);
 /* Store weights as bf16 (on = 1) or as f32 (on = 0).
@@ -267,7 +268,8 @@ FFWD_B200_API long long ffwd_b200_launch_count(void);
 /* Last error message of the calling thread ("" if none). */
 FFWD_B200_API const char *ffwd_b200_last_error(void);
 /* Precision plan chosen at load: 0 = single-pass bf16, 1 = single-pass f16,
- * 2 = split-bf16 2-pass, 3 = split-bf16 3-pass. */
+ * 2 = split-bf16 2-pass, 3 = split-bf16 3-pass, 4 = tf32 (kind::tf32 GEMMs over
+ * tf32-rounded f32 operands, f32 attention). */
 FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx);
 
 /* Host-side LPT partition used by the sharder: assigns each of n items with
@@ -281,6 +283,10 @@ FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts
  * 128 or 256.  x_lo / w_lo select the 2- / 3-pass split form when non-NULL. */
 FFWD_B200_API int ffwd_b200_gemm_bf16(const void *x, const void *x_lo, const void *w,
                                       const void *w_lo, float *y, int M, int N, int K, int bn);
+/* Y = X W^T in kind::tf32 (the tf32 plan's GEMM) on device pointers: f32 X [M, K],
+ * f32 W [N, K] (read as tf32), f32 Y [M, N]; K a multiple of 64, N of bn. */
+FFWD_B200_API int ffwd_b200_gemm_tf32(const float *x, const float *w, float *y, int M, int N, int K,
+                                      int bn);
 
 #ifdef __cplusplus
 }
