@@ -520,16 +520,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // ---------------------------------------------------------------- f32 path
 
 constexpr int kF32Threads = 128;
-constexpr int kF32Keys = 32;
+constexpr int kF32Keys = 32;  // keys per shared-memory block
+constexpr int kF32Dims = 32;  // dimensions per thread: D / 32 threads per query
 
-// TPQ threads cooperate on one query (each owns D / TPQ dimensions).
-template <int D, int TPQ>
+// CUDA-core attention for the exact plans (f32 scores and accumulation).  A
+// CTA takes kF32Threads * 32 / D queries of one head; each query's D
+// dimensions are split over D / 32 adjacent threads, thread `part` owning the
+// float4 chunks part, part + D / 32, ... (the chunks one shared-memory read
+// instruction touches are consecutive: no bank conflicts).  Keys and values pass
+// through shared memory 32 keys at a time; per block every thread computes its
+// 32 partial scores (broadcast float4 reads of K, reduced over the query's
+// threads by shuffles), takes the block maximum and rescales its running sum
+// and accumulator once, then accumulates exp2(s - m) V.  Scores are kept in
+// the log2 domain (scale * log2 e folded in), so each weight is one ex2.
+template <int D>
 __global__ void __launch_bounds__(kF32Threads)
     attn_f32_kernel(const AttnParams p) {
-    constexpr int DS = D / TPQ;
+    constexpr int TPQ = D / kF32Dims;
     constexpr int QT = kF32Threads / TPQ;
-    __shared__ float sk[kF32Keys][D];
-    __shared__ float sv[kF32Keys][D];
+    __shared__ __align__(16) float sk[kF32Keys][D];
+    __shared__ __align__(16) float sv[kF32Keys][D];
 
     const AttnItem item = p.items[blockIdx.x];
     const int h = blockIdx.y;
@@ -540,72 +550,102 @@ __global__ void __launch_bounds__(kF32Threads)
     const int part = threadIdx.x % TPQ;
     const bool qvalid = qi < L;
     const int kend = p.causal ? min(item.qt0 * QT + QT, L) : L;
+    const float sl2 = p.scale * 1.4426950408889634f;
 
-    float qv[DS], acc[DS];
+    float qv[kF32Dims], acc[kF32Dims];
     {
-        const float *qp = p.qkv_f32 + (size_t)(seq0 + (qvalid ? qi : 0)) * p.ldq + p.q_col0 + h * D +
-                          part * DS;
+        const float4 *qp = reinterpret_cast<const float4 *>(
+            p.qkv_f32 + (size_t)(seq0 + (qvalid ? qi : 0)) * p.ldq + p.q_col0 + h * D);
 #pragma unroll
-        for (int i = 0; i < DS; ++i) {
-            qv[i] = qp[i];
-            acc[i] = 0.0f;
+        for (int i = 0; i < kF32Dims / 4; ++i) {
+            const float4 v = qp[part + TPQ * i];
+            qv[4 * i] = v.x * sl2;
+            qv[4 * i + 1] = v.y * sl2;
+            qv[4 * i + 2] = v.z * sl2;
+            qv[4 * i + 3] = v.w * sl2;
         }
+#pragma unroll
+        for (int i = 0; i < kF32Dims; ++i) acc[i] = 0.0f;
     }
     float m = -INFINITY, l = 0.0f;
     for (int k0 = 0; k0 < kend; k0 += kF32Keys) {
         __syncthreads();
-        for (int idx = threadIdx.x; idx < kF32Keys * D; idx += kF32Threads) {
-            const int kr = idx / D, d = idx % D;
+        for (int idx = threadIdx.x; idx < kF32Keys * D / 4; idx += kF32Threads) {
+            const int kr = idx / (D / 4), d4 = idx % (D / 4);
             const int key = k0 + kr;
-            float kvv = 0.0f, vvv = 0.0f;
+            float4 kvv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vvv = kvv;
             if (key < L) {
                 const float *row = p.qkv_f32 + (size_t)(seq0 + key) * p.ldq;
-                kvv = row[p.k_col0 + kvh * D + d];
-                vvv = row[p.v_col0 + kvh * D + d];
+                kvv = *reinterpret_cast<const float4 *>(row + p.k_col0 + kvh * D + 4 * d4);
+                vvv = *reinterpret_cast<const float4 *>(row + p.v_col0 + kvh * D + 4 * d4);
             }
-            sk[kr][d] = kvv;
-            sv[kr][d] = vvv;
+            reinterpret_cast<float4 *>(sk[kr])[d4] = kvv;
+            reinterpret_cast<float4 *>(sv[kr])[d4] = vvv;
         }
         __syncthreads();
         const int nk = min(kF32Keys, kend - k0);
-        for (int kr = 0; kr < nk; ++kr) {
-            const int key = k0 + kr;
-            float dot = 0.0f;
+        float sc[kF32Keys];
+        float bmax = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < DS; ++i) dot += qv[i] * sk[kr][part * DS + i];
+        for (int j = 0; j < kF32Keys; ++j) {
+            const float4 *kr4 = reinterpret_cast<const float4 *>(&sk[j][0]) + part;
+            float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kF32Dims / 4; i += 2) {
+                const float4 a = kr4[TPQ * i], b = kr4[TPQ * (i + 1)];
+                d0 = fmaf(qv[4 * i], a.x, d0);
+                d1 = fmaf(qv[4 * i + 1], a.y, d1);
+                d0 = fmaf(qv[4 * i + 2], a.z, d0);
+                d1 = fmaf(qv[4 * i + 3], a.w, d1);
+                d0 = fmaf(qv[4 * i + 4], b.x, d0);
+                d1 = fmaf(qv[4 * i + 5], b.y, d1);
+                d0 = fmaf(qv[4 * i + 6], b.z, d0);
+                d1 = fmaf(qv[4 * i + 7], b.w, d1);
+            }
+            float dot = d0 + d1;
 #pragma unroll
             for (int o = 1; o < TPQ; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-            if (p.causal && key > qi) continue;
-            const float s = dot * p.scale;
-            // Online update in the order of libffwd/attn.c:72-91.
-            if (s > m) {
-                const float corr = expf(m - s);
-                l = l * corr + 1.0f;
+            const int key = k0 + j;
+            const bool vis = j < nk && (!p.causal || key <= qi);
+            sc[j] = vis ? dot : -INFINITY;
+            bmax = fmaxf(bmax, sc[j]);
+        }
+        const float m_new = fmaxf(m, bmax);
+        if (m_new == -INFINITY) continue;  // nothing visible yet
+        const float corr = ex2_approx(m - m_new);  // 0 on the first visible block
+        m = m_new;
+        l *= corr;
 #pragma unroll
-                for (int i = 0; i < DS; ++i) acc[i] = acc[i] * corr + sv[kr][part * DS + i];
-                m = s;
-            } else {
-                const float w = expf(s - m);
-                l += w;
+        for (int i = 0; i < kF32Dims; ++i) acc[i] *= corr;
 #pragma unroll
-                for (int i = 0; i < DS; ++i) acc[i] += w * sv[kr][part * DS + i];
+        for (int j = 0; j < kF32Keys; ++j) {
+            const float w = ex2_approx(sc[j] - m);
+            l += w;
+            const float4 *vr4 = reinterpret_cast<const float4 *>(&sv[j][0]) + part;
+#pragma unroll
+            for (int i = 0; i < kF32Dims / 4; ++i) {
+                const float4 v = vr4[TPQ * i];
+                acc[4 * i] = fmaf(w, v.x, acc[4 * i]);
+                acc[4 * i + 1] = fmaf(w, v.y, acc[4 * i + 1]);
+                acc[4 * i + 2] = fmaf(w, v.z, acc[4 * i + 2]);
+                acc[4 * i + 3] = fmaf(w, v.w, acc[4 * i + 3]);
             }
         }
     }
     if (!qvalid) return;
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-    const size_t off = (size_t)(seq0 + qi) * p.ldo + h * D + part * DS;
-    if (p.out_tf32) {
+    const size_t off = (size_t)(seq0 + qi) * p.ldo + h * D;
 #pragma unroll
-        for (int i = 0; i < DS; ++i) p.out_tf32[off + i] = round_tf32(acc[i] * inv);
-        return;
-    }
-#pragma unroll
-    for (int i = 0; i < DS; ++i) {
+    for (int i = 0; i < kF32Dims; ++i) {
+        const size_t o = off + 4 * (part + TPQ * (i / 4)) + (i % 4);  // dimension of acc[i]
         const float v = acc[i] * inv;
-        __nv_bfloat16 hi = __float2bfloat16_rn(v);
-        p.out_hi[off + i] = hi;
-        p.out_lo[off + i] = __float2bfloat16_rn(v - __bfloat162float(hi));
+        if (p.out_tf32) {
+            p.out_tf32[o] = round_tf32(v);
+        } else {
+            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+            p.out_hi[o] = hi;
+            p.out_lo[o] = __float2bfloat16_rn(v - __bfloat162float(hi));
+        }
     }
 }
 
@@ -642,15 +682,15 @@ int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStr
     return cudaGetLastError();
 }
 
-int attention_f32_qtile(int head_dim) { return head_dim > 64 ? kF32Threads / 2 : kF32Threads; }
+int attention_f32_qtile(int head_dim) { return kF32Threads * kF32Dims / head_dim; }
 
 int attention_f32_launch(const AttnParams &p, cudaStream_t stream) {
     if (p.n_items <= 0) return cudaSuccess;
     dim3 grid(p.n_items, p.n_heads);
     switch (p.head_dim) {
-    case 32: attn_f32_kernel<32, 1><<<grid, kF32Threads, 0, stream>>>(p); break;
-    case 64: attn_f32_kernel<64, 1><<<grid, kF32Threads, 0, stream>>>(p); break;
-    case 128: attn_f32_kernel<128, 2><<<grid, kF32Threads, 0, stream>>>(p); break;
+    case 32: attn_f32_kernel<32><<<grid, kF32Threads, 0, stream>>>(p); break;
+    case 64: attn_f32_kernel<64><<<grid, kF32Threads, 0, stream>>>(p); break;
+    case 128: attn_f32_kernel<128><<<grid, kF32Threads, 0, stream>>>(p); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
