@@ -118,18 +118,30 @@ class ClockSampler:
 
 
 class Dist:
-    def __init__(self):
+    """Rank plumbing of a torchrun launch (RANK / LOCAL_RANK / WORLD_SIZE /
+    MASTER_* from the environment): NCCL with one rank per GPU, or gloo on CPU
+    tensors (host-side tests).  Only the barrier and the max / sum of per-rank
+    scalars cross ranks; the data path has no collective."""
+
+    def __init__(self, backend: str = "nccl"):
         self.world = env_int("WORLD_SIZE", 1)
         self.rank = env_int("RANK", 0)
         self.local = env_int("LOCAL_RANK", 0)
+        self.backend = backend
         self.pg = False
 
     def init(self, torch):
         if self.world > 1:
             import torch.distributed as dist
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+            if self.backend == "nccl":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", device_id=torch.device("cuda", self.local))
+            else:
+                dist.init_process_group(self.backend)
             self.pg = True
+
+    def _device(self):
+        return "cuda" if self.backend == "nccl" else "cpu"
 
     def barrier(self, torch):
         if self.pg:
@@ -140,7 +152,7 @@ class Dist:
         if not self.pg:
             return v
         import torch.distributed as dist
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        t = torch.tensor([v], dtype=torch.float64, device=self._device())
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
@@ -148,7 +160,7 @@ class Dist:
         if not self.pg:
             return v
         import torch.distributed as dist
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        t = torch.tensor([v], dtype=torch.float64, device=self._device())
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
@@ -314,9 +326,7 @@ def run_ours(args, dist):
     dist.barrier(torch)
     clk = clocks.stop()
     local_s = e0.elapsed_time(e1) / 1000.0
-    max_s = dist.max(torch, local_s)
-    total_tokens = dist.sum(torch, float(T))
-    value = total_tokens * args.steps / max_s
+    value, max_s, total_tokens = whole_job_rate(dist, torch, T, args.steps, local_s)
     ms_per_step = 1000.0 * max_s / args.steps
 
     # ---------------- per-kernel timing (CUDA events on the backend's stream)
@@ -452,6 +462,14 @@ def run_ours(args, dist):
         print(json.dumps(line), flush=True)
     dist.close()
     return 0
+
+
+def whole_job_rate(dist, torch, tokens_per_step: int, steps: int, local_s: float):
+    """Weak-scaling aggregate: all ranks' tokens over the slowest rank's time.
+    Returns (tokens/s, max seconds over ranks, total tokens per step)."""
+    max_s = dist.max(torch, local_s)
+    total = dist.sum(torch, float(tokens_per_step))
+    return total * steps / max_s, max_s, total
 
 
 def main():
