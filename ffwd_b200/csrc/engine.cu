@@ -1398,6 +1398,32 @@ FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts
     return 0;
 }
 
+FFWD_B200_API int ffwd_b200_attention_items(int tc, int causal, int n_heads, int n_kv_heads,
+                                            int head_dim, const int *offsets, int batch,
+                                            int *items, int cap) {
+    if (batch < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || cap < 0 ||
+        (batch > 0 && !offsets) || (cap > 0 && !items))
+        return -1;
+    const int n = attention_count_items(tc != 0, n_heads, n_kv_heads, head_dim, offsets, batch);
+    if (n < 0) return -1;
+    if (!items) return n;
+    std::vector<AttnItem> v(std::max(n, 1));
+    const int got = attention_build_items(tc != 0, causal, n_heads, n_kv_heads, head_dim, offsets,
+                                          batch, v.data(), n);
+    if (got < 0 || got > cap) return -1;
+    for (int i = 0; i < got; ++i) {
+        const AttnItem &it = v[i];
+        int *o = items + 6 * i;
+        o[0] = it.seq;
+        o[1] = it.qt0;
+        o[2] = it.h0;
+        o[3] = it.qt1;
+        o[4] = it.h1;
+        o[5] = it.cost;
+    }
+    return got;
+}
+
 }  // extern "C"
 
 namespace fb {
