@@ -7,6 +7,7 @@ import collections
 
 import numpy as np
 import pytest
+from hypothesis import given, settings, strategies as st
 
 from ffwd_b200 import native
 
@@ -17,14 +18,11 @@ def tiles(L, t):
     return (L + t - 1) // t
 
 
-@pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("heads,kv,hd", [(16, 8, 128), (32, 8, 128), (12, 12, 64), (12, 12, 32),
-                                         (16, 16, 64)])
-def test_tensor_core_items_cover_once(causal, heads, kv, hd):
-    it = native.attention_items(LENS, heads, kv, hd, causal=causal, tc=True)
+def check_tc_cover(lens, heads, kv, hd, causal):
+    it = native.attention_items(lens, heads, kv, hd, causal=causal, tc=True)
     seen = collections.Counter()
     for seq, qt0, h0, qt1, h1, cost in it:
-        nq = tiles(LENS[seq], 128)
+        nq = tiles(lens[seq], 128)
         blocks = [(qt0, h0)] + ([(qt1, h1)] if qt1 >= 0 else [])
         for qt, h in blocks:
             assert 0 <= qt < nq and 0 <= h < heads
@@ -37,9 +35,25 @@ def test_tensor_core_items_cover_once(causal, heads, kv, hd):
             assert qt1 < 0 or (qt1 == qt0 and h1 == h0 + 1)
         else:            # one head: adjacent query tiles
             assert qt1 < 0 or (h1 == h0 and qt1 == qt0 + 1)
-    want = {(s, h, t) for s, L in enumerate(LENS) for h in range(heads)
+    want = {(s, h, t) for s, L in enumerate(lens) for h in range(heads)
             for t in range(tiles(L, 128))}
     assert set(seen) == want and max(seen.values()) == 1
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("heads,kv,hd", [(16, 8, 128), (32, 8, 128), (12, 12, 64), (12, 12, 32),
+                                         (16, 16, 64)])
+def test_tensor_core_items_cover_once(causal, heads, kv, hd):
+    check_tc_cover(LENS, heads, kv, hd, causal)
+
+
+@settings(max_examples=60, deadline=None)
+@given(lens=st.lists(st.integers(1, 3000), min_size=1, max_size=24),
+       layout=st.sampled_from([(16, 8, 128), (32, 8, 128), (12, 12, 64), (16, 16, 32),
+                               (14, 2, 64), (24, 8, 128)]),
+       causal=st.booleans())
+def test_tensor_core_items_cover_once_random(lens, layout, causal):
+    check_tc_cover(lens, *layout, causal)
 
 
 def test_tensor_core_item_order():
