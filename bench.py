@@ -22,7 +22,6 @@ import argparse
 import ctypes
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -129,6 +128,7 @@ class Dist:
         self.local = env_int("LOCAL_RANK", 0)
         self.backend = backend
         self.pg = False
+        self._gloo = None
 
     def init(self, torch):
         if self.world > 1:
@@ -164,6 +164,15 @@ class Dist:
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
+    def cpu_barrier(self):
+        """Barrier over a gloo group: waiting ranks spin on the host, not on a
+        collective kernel that would hold SMs of their GPU."""
+        if self.pg:
+            import torch.distributed as dist
+            if self._gloo is None:
+                self._gloo = dist.new_group(backend="gloo")
+            dist.barrier(group=self._gloo)
+
     def close(self):
         if self.pg:
             import torch.distributed as dist
@@ -173,33 +182,68 @@ class Dist:
 # ------------------------------------------------------------------ CPU reference
 
 
-def cpu_reference_sample(model_dir, seqs, budget_s):
-    """Time the reference CPU path on the leading sequences of the batch that
-    fit ~budget_s.  Returns (tokens/s, tokens, seconds, n_seqs, threads)."""
+def cpu_info():
+    """CPU model name, logical and physical core counts of this host."""
+    name = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                name = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    logical = os.cpu_count() or 1
+    try:
+        import psutil
+        physical = psutil.cpu_count(logical=False) or logical
+    except Exception:
+        physical = logical
+    return {"model": name, "nproc": logical, "physical_cores": physical}
+
+
+def cpu_reference_sample(model_dir, seqs, budget_s, repeats=5, min_seqs=2):
+    """Time the reference CPU path on the leading sequences of the batch (at
+    least min_seqs of them) sized so `repeats` runs take about budget_s.
+    Returns (median tokens/s, tokens, median seconds, n_seqs, threads, outputs
+    of the sample, [tokens/s of every run])."""
     from oracle.ref import RefModel
     threads = os.cpu_count() or 1
     ref = RefModel(model_dir, threads=threads)
     probe = [seqs[0][:64]]
-    t0 = time.perf_counter()
     ref.encode_batch(probe)  # warm-up: page in the weights
     t0 = time.perf_counter()
     ref.encode_batch(probe)
     per_tok = (time.perf_counter() - t0) / len(probe[0])
+    per_run = budget_s / repeats
     n, tok = 0, 0
     while n < len(seqs):
         L = len(seqs[n])
-        # attention grows with L; scale the probe rate by length / 64 beyond the linear part
+        # attention grows with L; scale the probe rate by length / 4096 beyond the linear part
         est = per_tok * (tok + L) * (1.0 + (tok + L) / 4096.0)
-        if n > 0 and est > budget_s:
+        if n >= min_seqs and est > per_run:
             break
         tok += L
         n += 1
     sample = seqs[:n]
-    t0 = time.perf_counter()
-    ref.encode_batch(sample)
-    dt = time.perf_counter() - t0
+    rates, times, outs = [], [], None
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        outs = ref.encode_batch(sample)
+        dt = time.perf_counter() - t0
+        times.append(dt)
+        rates.append(tok / dt)
     ref.close()
-    return tok / dt, tok, dt, n, threads
+    return (statistics.median(rates), tok, statistics.median(times), n, threads, outs, rates)
+
+
+def parity_rows(gpu_rows, ref_rows):
+    """Row-by-row agreement of GPU pooled rows with the reference CPU path."""
+    a = np.asarray(gpu_rows, np.float64)
+    b = np.asarray(ref_rows, np.float64)
+    cos = (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+    return {"rows": int(len(a)), "min_cos": float(cos.min()),
+            "max_abs": float(np.abs(a - b).max()), "gate_cos": 0.999,
+            "ok": bool(np.isfinite(a).all() and cos.min() >= 0.999)}
 
 
 def run_reference(args, dist):
@@ -238,6 +282,7 @@ def run_reference(args, dist):
         ref.encode_batch(sample)
         times.append(time.perf_counter() - t0)
     ref.close()
+    info = cpu_info()
     total = sum(times)
     value = tok * len(times) / total
     sample_desc = (f"first {n} of the 128 seeded sequences ({tok} tokens) per step, "
@@ -250,7 +295,9 @@ def run_reference(args, dist):
         "config": {"workload": "Qwen3-Embedding-0.6B bf16, 128 seqs U[32,2048]+EOS, last-token+L2",
                    "sample_tokens_per_step": tok},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
-                         "sample": sample_desc},
+                         "sample": sample_desc, "cpu_model": info["model"],
+                         "nproc": info["nproc"], "physical_cores": info["physical_cores"],
+                         "median_step_tokens_per_s": tok / statistics.median(times)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -260,14 +307,11 @@ def run_reference(args, dist):
 # ------------------------------------------------------------------ ours
 
 
-def read_traffic():
-    """DRAM bytes per launch of the gate/up GEMM from the committed ncu summary
-    (profiles/gemm_gate_up_qwen3_0.6b.md, key `dram_bytes_per_token`)."""
-    p = os.path.join(ROOT, "profiles", "gemm_gate_up_qwen3_0.6b.md")
-    if not os.path.exists(p):
-        return None
-    m = re.search(r"dram_bytes_per_token\s*[:=]\s*([0-9.eE+-]+)", open(p).read())
-    return float(m.group(1)) if m else None
+# DRAM bytes (read + write) per token of one gate/up GEMM launch, from an ncu
+# capture of that kernel (profiles/gemm_gate_up_qwen3_0.6b.md gives the
+# command and the raw figures); roofline.traffic scales it by the step's
+# tokens.  Refresh it whenever the kernel changes.
+GATE_UP_DRAM_BYTES_PER_TOKEN = 7992.0
 
 
 def run_ours(args, dist):
@@ -348,7 +392,7 @@ def run_ours(args, dist):
     gu_flops = 2.0 * T * (2 * spec.intermediate) * H
     gu_s = op_ms["gemm_gate_up_swiglu"] / 1000.0
     achieved = gu_flops / gu_s / 1e12
-    traffic_per_tok = read_traffic()
+    traffic_per_tok = GATE_UP_DRAM_BYTES_PER_TOKEN
     fpt, lin_fpt, attn_fpt = flops_per_token(spec, seqs)
     kernels = {
         "gemm_qkv_qknorm_rope": 2.0 * T * (q + 2 * kv) * H,
@@ -366,6 +410,41 @@ def run_ours(args, dist):
     kernel_report["rmsnorm"] = {"ms": round(op_ms["rmsnorm"], 4),
                                 "gbs": round(T * H * 6 / (op_ms["rmsnorm"] / 1000.0) / 1e9, 1)}
     model_tflops = T * fpt / (ms_per_step / 1000.0) / 1e12
+
+    # ---------------- where one step's time goes (CUDA events, same stream)
+    def timed(fn, reps=1):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b) / reps
+
+    def layer_stack():
+        for li in range(spec.n_layers):
+            for op in range(7):
+                m.run_op(op, layer=li)
+
+    embed_ms = timed(lambda: m.run_op(7), reps)
+    pool_ms = timed(lambda: m.run_op(8), reps)
+    layer_stack()
+    stack_ms = timed(layer_stack, 2)
+    ops_sum_ms = spec.n_layers * sum(op_ms[ops[o]] for o in (0, 1, 2, 4, 5)) \
+        + spec.n_layers * 2 * op_ms["rmsnorm"]
+    step_split = {
+        "step_ms": round(ms_per_step, 3),
+        "embedding_ms": round(embed_ms, 3),
+        "layer_stack_ms": round(stack_ms, 3),
+        "per_op_sum_ms": round(ops_sum_ms, 3),
+        "pool_ms": round(pool_ms, 3),
+        "host_and_gaps_ms": round(ms_per_step - embed_ms - stack_ms - pool_ms, 3),
+        "note": "layer_stack re-issues the 28 x 7 layer launches back to back; per_op_sum is "
+                "28 x the per-op times measured in isolation; host_and_gaps = step - embedding "
+                "- layer stack - pool (host work list, H2D of ids/offsets/items, sync)",
+    }
+    gpu_rows = d_out.cpu().numpy()
 
     # ---------------- end to end through the public API (host buffers)
     os.environ["FFWD_B200_DEVICES"] = str(dev)
@@ -419,16 +498,39 @@ def run_ours(args, dist):
         lat.append((time.perf_counter() - t0) * 1000.0)
     api.close()
 
-    # ---------------- CPU baseline (rank 0, N = 1)
-    cpu = None
-    if dist.world == 1 and not args.no_cpu:
+    # ---------------- CPU baseline and parity (rank 0): the reference CPU path on
+    # the leading sequences of this rank's batch, its rows compared with ours.
+    cpu, parity = None, None
+    if dist.rank == 0 and not args.no_cpu:
         from oracle import ref as oref
         if oref.available():
-            v, tok, dt, n, thr = cpu_reference_sample(d, seqs, budget_s=args.cpu_budget)
-            cpu = {"value": v, "unit": UNIT, "cores": thr, "kind": "reference",
-                   "sample": f"first {n} of the 128 seeded sequences ({tok} tokens, {dt:.1f} s), "
-                             f"reference CPU path (OpenBLAS f32) via oracle/_ref"}
+            budget = args.cpu_budget if dist.world == 1 else 4.0
+            reps = 5 if dist.world == 1 else 1
+            v, tok, dt, n, thr, ref_rows, rates = cpu_reference_sample(d, seqs, budget, reps)
+            parity = parity_rows(gpu_rows[:n], ref_rows)
+            parity["sequences"] = f"first {n} of the bench batch ({tok} tokens), 28 layers, " \
+                                  "vocab 151669, vs the reference CPU path (oracle/_ref)"
+            if dist.world == 1:
+                info = cpu_info()
+                cpu = {"value": v, "unit": UNIT, "cores": thr, "kind": "reference",
+                       "sample": f"first {n} of the 128 seeded sequences ({tok} tokens, "
+                                 f"median {dt:.1f} s of {reps} runs), reference CPU path "
+                                 f"(OpenBLAS f32) via oracle/_ref",
+                       "runs_tokens_per_s": [round(r, 1) for r in rates],
+                       "cpu_model": info["model"], "nproc": info["nproc"],
+                       "physical_cores": info["physical_cores"]}
+        else:
+            parity = {"ok": False, "error": "oracle/_ref/libffwd_ref.so not built"}
 
+    # ---------------- the library's own multi-GPU sharder (N > 1): rank 0 encodes
+    # all ranks' batches in one ffwd_encode_batch call over devices 0..N-1 while
+    # the other ranks wait on a CPU (gloo) barrier, so no collective kernel
+    # occupies their GPUs.
+    sharded = None
+    if dist.world > 1 and not args.no_sharded:
+        if dist.rank == 0:
+            sharded = sharded_leg(d, spec, dist.world, args)
+        dist.cpu_barrier()
     if dist.rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world,
@@ -450,9 +552,14 @@ def run_ours(args, dist):
                 "bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                 "frac": achieved / peak_tflops, "peak_source": peak_kind,
                 "flops_per_launch": gu_flops,
-                "traffic": (traffic_per_tok * T) if traffic_per_tok else None,
+                "traffic": traffic_per_tok * T,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                  "gate/up launch, per token, scaled to this step's tokens",
             },
             "kernels": kernel_report,
+            "step_split": step_split,
+            "parity": parity,
+            "sharded_e2e": sharded,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "ffwd_encode_batch (libffwd_b200_api.so)"},
             "gpu_launches": launches,
@@ -461,7 +568,42 @@ def run_ours(args, dist):
         }
         print(json.dumps(line), flush=True)
     dist.close()
+    if parity is not None and not parity.get("ok"):
+        sys.stderr.write(f"parity check failed: {parity}\n")
+        return 1
     return 0
+
+
+def sharded_leg(d, spec, world, args):
+    """ffwd_encode_batch of all ranks' batches (world x 128 sequences) through
+    the public API with FFWD_B200_DEVICES=0..world-1: the library's LPT
+    sharder, one host thread and stream per GPU, rows copied into the
+    caller's buffer."""
+    from ffwd_b200 import native
+    os.environ["FFWD_B200_DEVICES"] = ",".join(str(i) for i in range(world))
+    seqs = []
+    for r in range(world):
+        seqs += synth.token_batch(CONFIG, seed=1 + r)
+    api = native.FfwdApi(d, gemm_mode="bf16")
+    ins, keep = native._pack_inputs(seqs)
+    out = np.zeros((len(seqs), spec.hidden), np.float32)
+    for _ in range(2):
+        assert api.encode_batch_into(ins, len(seqs), out.ctypes.data) == 0
+    steps = max(1, args.steps)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        assert api.encode_batch_into(ins, len(seqs), out.ctypes.data) == 0
+    dt = (time.perf_counter() - t0) / steps
+    st = api.shard_stats()
+    api.close()
+    tokens = sum(len(q) for q in seqs)
+    ms = [x[2] for x in st]
+    return {"value": tokens / dt, "unit": UNIT, "n_devices": world, "sequences": len(seqs),
+            "tokens_per_call": tokens, "ms_per_call": 1000.0 * dt, "calls": steps,
+            "per_device": [{"seqs": a, "tokens": b, "ms": round(c, 2)} for a, b, c in st],
+            "imbalance_max_over_mean": max(ms) / (sum(ms) / len(ms)) if ms else None,
+            "api": "ffwd_encode_batch (libffwd_b200_api.so), FFWD_B200_DEVICES=0..N-1, host "
+                   "buffers, wall clock of the synchronous call"}
 
 
 def whole_job_rate(dist, torch, tokens_per_step: int, steps: int, local_s: float):
@@ -480,6 +622,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the multi-GPU sharder leg (N > 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

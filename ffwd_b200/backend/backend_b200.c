@@ -51,6 +51,8 @@ FFWD_B200_API int ffwd_init(const ffwd_options_t *opts, char *err, size_t errlen
     return 0;
 }
 
+FFWD_B200_API ffwd_b200_ctx_t *ffwd_b200_api_context(ffwd_t *b) { return b ? b->ctx : NULL; }
+
 FFWD_B200_API ffwd_t *ffwd_open(const char *model_dir, int is_late, const ffwd_options_t *opts,
                                 char *err, size_t errlen) {
     (void)opts;

@@ -18,6 +18,7 @@
 #include "rowops.cuh"
 
 #include <algorithm>
+#include <chrono>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -43,6 +44,11 @@ std::vector<int> g_devices;
 bool g_devices_set = false;
 int g_max_tokens = 262144;
 thread_local std::string t_err;
+// Host-side fault injection (ffwd_b200_test_inject): the device entry whose
+// next shard fails before launch, and how many of the next workspace
+// allocations fail.
+std::atomic<int> g_inject_shard{-1};
+std::atomic<int> g_inject_alloc{0};
 
 void fail(const char *fmt, ...) {
     char buf[512];
@@ -188,7 +194,9 @@ enum Op : int {
     kOpUp = 4,
     kOpDown = 5,
     kOpNorm2 = 6,
-    kOpCount = 7,
+    kOpCount = 7,  // ops of one layer
+    kOpEmbed = 7,  // positions + embedding (+ first norm), re-issued by ffwd_b200_run_op
+    kOpPool = 8,   // pooling (+ final norm, L2) into ws.pooled, likewise
 };
 
 struct Device {
@@ -236,6 +244,14 @@ struct ffwd_b200_ctx {
     std::vector<fb::Device> devs;
     float lin_flops_per_token = 0.0f;
     int token_dim = 0;  // late interaction: 1_Dense output width (0: pooled model)
+    // Per device entry, the last encode_batch's share: sequences, tokens and
+    // the host wall time of that shard's worker (packing to copied-out rows).
+    struct Shard {
+        int seqs = 0;
+        long long tokens = 0;
+        double ms = 0.0;
+    };
+    std::vector<Shard> last_shards;
 };
 
 // A late-interaction model: the base model context plus its 1_Dense head (on
@@ -456,10 +472,16 @@ struct HostModel {
     SafeTensors st;
 };
 
+int noalloc_scratch(int dev, uint8_t **out);
+
 int load_device(HostModel &hm, Device &D, std::string &err) {
     const ffwd_config_t &c = hm.cfg;
     CK(cudaSetDevice(D.dev));
     CK(cudaStreamCreateWithFlags(&D.stream, cudaStreamNonBlocking));
+    // Resolve the no-allocation arena now, so its module (and the arena) is
+    // loaded when the model is, not on the first no-allocation request.
+    uint8_t *arena = nullptr;
+    if (noalloc_scratch(D.dev, &arena)) return -1;
     CK(cudaDeviceGetAttribute(&D.num_sms, cudaDevAttrMultiProcessorCount, D.dev));
     const bool split_w = hm.prec == 3;
     const int H = c.hidden_size, I = c.intermediate_size;
@@ -612,6 +634,37 @@ void free_device(Device &D) {
 
 // ------------------------------------------------------------------ workspace
 
+// Device and pinned allocations of the workspace.  ffwd_b200_test_inject can
+// make the next ones fail, to exercise the out-of-memory paths.
+cudaError_t ws_malloc(void **p, size_t bytes) {
+    if (g_inject_alloc.load() > 0 && g_inject_alloc.fetch_sub(1) > 0) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMalloc(p, bytes);
+}
+
+cudaError_t ws_malloc_host(void **p, size_t bytes) {
+    if (g_inject_alloc.load() > 0 && g_inject_alloc.fetch_sub(1) > 0) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMallocHost(p, bytes);
+}
+
+template <typename T>
+int ws_free(T **p, bool host = false) {
+    if (*p) {
+        cudaError_t e = host ? cudaFreeHost(*p) : cudaFree(*p);
+        *p = nullptr;
+        CK(e);
+    }
+    return 0;
+}
+
+// Grow the workspace to T packed rows, B sequences, n_items attention items
+// and n_spans spans.  A capacity is set only once all of its buffers exist,
+// so a failed allocation leaves it at 0 and the next call allocates again.
 int ensure_ws(ffwd_b200_ctx *ctx, Device &D, int T, int B, int n_items, int n_spans) {
     Workspace &w = D.ws;
     const ffwd_config_t &c = ctx->cfg;
@@ -621,83 +674,92 @@ int ensure_ws(ffwd_b200_ctx *ctx, Device &D, int T, int B, int n_items, int n_sp
     if (T > w.cap_t) {
         CK(cudaStreamSynchronize(D.stream));
         const int cap = std::max(T, std::min(g_max_tokens, std::max(T, 2 * w.cap_t)));
+        w.cap_t = 0;
         void **bufs[] = {(void **)&w.ids, (void **)&w.pos, (void **)&w.x, (void **)&w.xb,
                          (void **)&w.xb_lo, &w.qkv, (void **)&w.att, (void **)&w.att_lo,
                          (void **)&w.hmid, (void **)&w.hmid_lo};
         for (void **b : bufs)
-            if (*b) {
-                CK(cudaFree(*b));
-                *b = nullptr;
-            }
-        if (w.h_ids) CK(cudaFreeHost(w.h_ids));
+            if (ws_free(b)) return -1;
+        if (ws_free(&w.h_ids, true)) return -1;
         const size_t t = (size_t)cap;
         const int H = c.hidden_size, qkv = c.q_dim + 2 * c.kv_dim;
         const int inter = c.intermediate_size;
-        CK(cudaMalloc(&w.ids, t * 4));
-        CK(cudaMalloc(&w.pos, t * 4));
-        CK(cudaMalloc(&w.x, t * H * 4));
-        CK(cudaMalloc(&w.xb, t * H * ob));
-        CK(cudaMalloc(&w.qkv, t * qkv * (exact ? 4 : 2)));
-        CK(cudaMalloc(&w.att, t * c.q_dim * ob));
-        CK(cudaMalloc(&w.hmid, t * inter * ob));
+        CK(ws_malloc((void **)&w.ids, t * 4));
+        CK(ws_malloc((void **)&w.pos, t * 4));
+        CK(ws_malloc((void **)&w.x, t * H * 4));
+        CK(ws_malloc((void **)&w.xb, t * H * ob));
+        CK(ws_malloc(&w.qkv, t * qkv * (exact ? 4 : 2)));
+        CK(ws_malloc((void **)&w.att, t * c.q_dim * ob));
+        CK(ws_malloc((void **)&w.hmid, t * inter * ob));
         if (split) {
-            CK(cudaMalloc(&w.xb_lo, t * H * 2));
-            CK(cudaMalloc(&w.att_lo, t * c.q_dim * 2));
-            CK(cudaMalloc(&w.hmid_lo, t * inter * 2));
+            CK(ws_malloc((void **)&w.xb_lo, t * H * 2));
+            CK(ws_malloc((void **)&w.att_lo, t * c.q_dim * 2));
+            CK(ws_malloc((void **)&w.hmid_lo, t * inter * 2));
         }
-        CK(cudaMallocHost(&w.h_ids, t * 4));
+        CK(ws_malloc_host((void **)&w.h_ids, t * 4));
         w.cap_t = cap;
     }
-    if (B + 1 > w.cap_b) {
+    // Pooled rows serve sequences and spans alike: size them for both.
+    const int rows = std::max(B + 1, n_spans + 1);
+    if (rows > w.cap_b) {
         CK(cudaStreamSynchronize(D.stream));
-        const int cap = std::max(B + 1, 2 * w.cap_b);
-        if (w.offsets) CK(cudaFree(w.offsets));
-        if (w.pooled) CK(cudaFree(w.pooled));
-        if (w.h_offsets) CK(cudaFreeHost(w.h_offsets));
-        if (w.h_out) CK(cudaFreeHost(w.h_out));
-        CK(cudaMalloc(&w.offsets, (size_t)cap * 4));
-        CK(cudaMalloc(&w.pooled, (size_t)cap * c.hidden_size * 4));
-        CK(cudaMallocHost(&w.h_offsets, (size_t)cap * 4));
-        CK(cudaMallocHost(&w.h_out, (size_t)cap * c.hidden_size * 4));
+        const int cap = std::max(rows, 2 * w.cap_b);
+        w.cap_b = 0;
+        if (ws_free(&w.offsets) || ws_free(&w.pooled) || ws_free(&w.h_offsets, true) ||
+            ws_free(&w.h_out, true))
+            return -1;
+        CK(ws_malloc((void **)&w.offsets, (size_t)cap * 4));
+        CK(ws_malloc((void **)&w.pooled, (size_t)cap * c.hidden_size * 4));
+        CK(ws_malloc_host((void **)&w.h_offsets, (size_t)cap * 4));
+        CK(ws_malloc_host((void **)&w.h_out, (size_t)cap * c.hidden_size * 4));
         w.cap_b = cap;
     }
     if (n_items > w.cap_items) {
         CK(cudaStreamSynchronize(D.stream));
         const int cap = std::max(n_items, 2 * w.cap_items);
-        if (w.items) CK(cudaFree(w.items));
-        if (w.h_items) CK(cudaFreeHost(w.h_items));
-        CK(cudaMalloc(&w.items, (size_t)cap * sizeof(AttnItem)));
-        CK(cudaMallocHost(&w.h_items, (size_t)cap * sizeof(AttnItem)));
+        w.cap_items = 0;
+        if (ws_free(&w.items) || ws_free(&w.h_items, true)) return -1;
+        CK(ws_malloc((void **)&w.items, (size_t)cap * sizeof(AttnItem)));
+        CK(ws_malloc_host((void **)&w.h_items, (size_t)cap * sizeof(AttnItem)));
         w.cap_items = cap;
     }
     if (n_spans > w.cap_spans) {
         CK(cudaStreamSynchronize(D.stream));
         const int cap = std::max(n_spans, 2 * w.cap_spans);
-        if (w.span_starts) CK(cudaFree(w.span_starts));
-        if (w.span_ends) CK(cudaFree(w.span_ends));
-        if (w.h_spans) CK(cudaFreeHost(w.h_spans));
-        CK(cudaMalloc(&w.span_starts, (size_t)cap * 4));
-        CK(cudaMalloc(&w.span_ends, (size_t)cap * 4));
-        CK(cudaMallocHost(&w.h_spans, (size_t)cap * 2 * 4));
-        if (w.pooled && n_spans + 1 > w.cap_b) {
-            CK(cudaFree(w.pooled));
-            CK(cudaFreeHost(w.h_out));
-            CK(cudaMalloc(&w.pooled, (size_t)cap * c.hidden_size * 4));
-            CK(cudaMallocHost(&w.h_out, (size_t)cap * c.hidden_size * 4));
-            w.cap_b = cap;
-        }
+        w.cap_spans = 0;
+        if (ws_free(&w.span_starts) || ws_free(&w.span_ends) || ws_free(&w.h_spans, true))
+            return -1;
+        CK(ws_malloc((void **)&w.span_starts, (size_t)cap * 4));
+        CK(ws_malloc((void **)&w.span_ends, (size_t)cap * 4));
+        CK(ws_malloc_host((void **)&w.h_spans, (size_t)cap * 2 * 4));
         w.cap_spans = cap;
     }
-    if (!w.err) {
+    if (!w.err || !w.h_err) {
         // err[0]: device error word; err[2..3]: attention scheduler counters.
-        CK(cudaMalloc(&w.err, 16));
+        if (ws_free(&w.err) || ws_free(&w.h_err, true)) return -1;
+        CK(ws_malloc((void **)&w.err, 16));
         CK(cudaMemset(w.err, 0, 16));
-        CK(cudaMallocHost(&w.h_err, 4));
+        CK(ws_malloc_host((void **)&w.h_err, 4));
     }
     return 0;
 }
 
 // ------------------------------------------------------------------ forward
+
+// Self-test of the bounded wait: one thread waits on an mbarrier that nothing
+// ever arrives at, with a short limit; the wait records kErrWaitTimeout and
+// the kernel returns.
+__global__ void wait_selftest_kernel(int *err, uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, err, &abort_flag, limit_ns);
+}
 
 __global__ void positions_kernel(const int *offsets, int pos_offset, int *pos) {
     const int b = blockIdx.x;
@@ -769,41 +831,17 @@ int make_act_maps(const ffwd_b200_ctx *ctx, FwdState &fs, const Workspace &w, in
                : 0;
 }
 
-// Upload-independent preparation: RoPE cache, attention items, tensor maps,
-// positions and the embedding (+ first norm).  ws.ids / ws.offsets must hold
-// the packed batch; h_offsets is its host copy.
-int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int *h_offsets) {
+int embed_step(ffwd_b200_ctx *ctx, Device &D, const FwdState &fs, Workspace &w);
+
+// Tensor maps, attention parameters, positions and the embedding (+ first
+// norm) of one forward over the buffers of workspace w, whose ids, offsets and
+// items (fs.n_items of them) already hold the packed batch (or are queued on
+// D.stream before this).
+int setup_forward(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, Workspace &w, int T, int B) {
     const ffwd_config_t &c = ctx->cfg;
-    Workspace &w = D.ws;
-    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
-    const bool split = ctx->prec == 2 || ctx->prec == 3;
-    const int H = c.hidden_size;
     const int qkv_dim = c.q_dim + 2 * c.kv_dim;
-    const bool bert = c.family == FFWD_FAMILY_BERT;
-    const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
-    cudaStream_t s = D.stream;
     fs.T = T;
     fs.B = B;
-
-    int max_len = 0;
-    for (int b = 0; b < B; ++b) max_len = std::max(max_len, h_offsets[b + 1] - h_offsets[b]);
-    if (!bert && ensure_rope(D, c, max_len)) return -1;
-
-    // Attention work list, heaviest first.
-    {
-        const int n = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B);
-        if (n < 0 || ensure_ws(ctx, D, T, B, n, 0)) return -1;
-        fs.n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
-                                           c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B,
-                                           w.h_items, w.cap_items);
-        if (fs.n_items < 0) {
-            fail("attention work list overflow");
-            return -1;
-        }
-        CK(cudaMemcpyAsync(w.items, w.h_items, (size_t)fs.n_items * sizeof(AttnItem),
-                           cudaMemcpyHostToDevice, s));
-    }
-
     if (make_act_maps(ctx, fs, w, T)) return -1;
 
     AttnParams &ap = fs.ap;
@@ -830,6 +868,17 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
     ap.f16 = ctx->f16 ? 1 : 0;
     ap.out_tf32 = ctx->prec == 4 ? reinterpret_cast<float *>(w.att) : nullptr;
 
+    return embed_step(ctx, D, fs, w);
+}
+
+// Positions and the embedding (+ first norm) of the forward fs over w.
+int embed_step(ffwd_b200_ctx *ctx, Device &D, const FwdState &fs, Workspace &w) {
+    const ffwd_config_t &c = ctx->cfg;
+    const bool split = ctx->prec == 2 || ctx->prec == 3;
+    const int H = c.hidden_size, T = fs.T, B = fs.B;
+    const bool bert = c.family == FFWD_FAMILY_BERT;
+    const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
+    cudaStream_t s = D.stream;
     const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0,
                         ctx->prec == 4 ? reinterpret_cast<float *>(w.xb) : nullptr};
     LAUNCH((positions_kernel<<<B, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0, w.pos),
@@ -841,6 +890,38 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
         LAUNCH(embed_rms_launch(w.ids, T, D.embed, D.embed_bf16, c.vocab_size, H, w.x,
                                 D.layers[0].in_norm, eps, xb_out, w.err, s));
     return 0;
+}
+
+// Upload-independent preparation: RoPE cache, attention items, tensor maps,
+// positions and the embedding (+ first norm).  ws.ids / ws.offsets must hold
+// the packed batch; h_offsets is its host copy.
+int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int *h_offsets) {
+    const ffwd_config_t &c = ctx->cfg;
+    Workspace &w = D.ws;
+    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
+    const bool bert = c.family == FFWD_FAMILY_BERT;
+    cudaStream_t s = D.stream;
+
+    int max_len = 0;
+    for (int b = 0; b < B; ++b) max_len = std::max(max_len, h_offsets[b + 1] - h_offsets[b]);
+    if (!bert && ensure_rope(D, c, max_len)) return -1;
+
+    // Attention work list, heaviest first.
+    {
+        const int n = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B);
+        if (n < 0 || ensure_ws(ctx, D, T, B, n, 0)) return -1;
+        fs.n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
+                                           c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B,
+                                           w.h_items, w.cap_items);
+        if (fs.n_items < 0) {
+            fail("attention work list overflow");
+            return -1;
+        }
+        CK(cudaMemcpyAsync(w.items, w.h_items, (size_t)fs.n_items * sizeof(AttnItem),
+                           cudaMemcpyHostToDevice, s));
+    }
+
+    return setup_forward(ctx, D, fs, w, T, B);
 }
 
 // One op of layer li on the prepared forward.
@@ -1006,6 +1087,13 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
     const int H = c.hidden_size;
     const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
     CK(cudaSetDevice(D.dev));
+    {
+        int entry = (int)(&D - ctx->devs.data());
+        if (g_inject_shard.compare_exchange_strong(entry, -1)) {
+            fail("injected failure of the shard on device entry %d", entry);
+            return -1;
+        }
+    }
     // Forwards of at most g_max_tokens rows, sized evenly: with n forwards
     // needed, each aims at total / n tokens, so no small tail forward runs
     // the whole layer stack for a few sequences.
@@ -1432,24 +1520,36 @@ namespace {
 int encode_batch_impl(ffwd_b200_ctx_t *ctx, const ffwd_input_t *inputs, int batch, void *out,
                       const OutSpec &os) {
     const int nd = (int)ctx->devs.size();
-    if (nd == 1) {
-        std::vector<int> idx(batch);
-        std::iota(idx.begin(), idx.end(), 0);
-        return run_on_device(ctx, ctx->devs[0], inputs, idx, out, os);
-    }
-    std::vector<double> cost(batch);
-    for (int b = 0; b < batch; ++b) cost[b] = seq_cost(ctx, inputs[b].n_tokens);
-    std::vector<int> part(batch);
-    ffwd_b200_lpt_partition(cost.data(), batch, nd, part.data());
+    ctx->last_shards.assign(nd, ffwd_b200_ctx::Shard{});
     std::vector<std::vector<int>> idx(nd);
-    for (int b = 0; b < batch; ++b) idx[part[b]].push_back(b);
+    if (nd == 1) {
+        idx[0].resize(batch);
+        std::iota(idx[0].begin(), idx[0].end(), 0);
+    } else {
+        std::vector<double> cost(batch);
+        for (int b = 0; b < batch; ++b) cost[b] = seq_cost(ctx, inputs[b].n_tokens);
+        std::vector<int> part(batch);
+        ffwd_b200_lpt_partition(cost.data(), batch, nd, part.data());
+        for (int b = 0; b < batch; ++b) idx[part[b]].push_back(b);
+    }
+    auto run = [&](int d) {
+        auto &sh = ctx->last_shards[d];
+        sh.seqs = (int)idx[d].size();
+        for (int i : idx[d]) sh.tokens += inputs[i].n_tokens;
+        const auto t0 = std::chrono::steady_clock::now();
+        const int rc = run_on_device(ctx, ctx->devs[d], inputs, idx[d], out, os);
+        sh.ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0)
+                    .count();
+        return rc;
+    };
+    if (nd == 1) return run(0);
     std::vector<int> rc(nd, 0);
     std::vector<std::string> errs(nd);
     std::vector<std::thread> th;
     for (int d = 0; d < nd; ++d) {
         if (idx[d].empty()) continue;
         th.emplace_back([&, d] {
-            rc[d] = run_on_device(ctx, ctx->devs[d], inputs, idx[d], out, os);
+            rc[d] = run(d);
             errs[d] = t_err;
         });
     }
@@ -1592,6 +1692,10 @@ FFWD_B200_API int ffwd_b200_encode_spans_batch(ffwd_b200_ctx_t *ctx,
 FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const int *d_ids,
                                           const int *h_offsets, int batch, float *d_out, int sync) {
     t_err.clear();
+    if (h_offsets && batch > 0 && h_offsets[0] != 0) {
+        fail("row offsets must start at 0 (got %d)", h_offsets[0]);
+        return -1;
+    }
     if (!ctx || dev < 0 || dev >= (int)ctx->devs.size() || !d_ids || !h_offsets || batch <= 0 ||
         !d_out) {
         fail("invalid arguments");
@@ -1630,7 +1734,7 @@ FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const i
 
 FFWD_B200_API int ffwd_b200_run_op(ffwd_b200_ctx_t *ctx, int dev, int op, int layer, int reps) {
     t_err.clear();
-    if (!ctx || dev < 0 || dev >= (int)ctx->devs.size() || op < 0 || op >= kOpCount || layer < 0 ||
+    if (!ctx || dev < 0 || dev >= (int)ctx->devs.size() || op < 0 || op > kOpPool || layer < 0 ||
         layer >= ctx->cfg.n_layers || reps < 1) {
         fail("invalid arguments");
         return -1;
@@ -1641,8 +1745,73 @@ FFWD_B200_API int ffwd_b200_run_op(ffwd_b200_ctx_t *ctx, int dev, int op, int la
         return -1;
     }
     CK(cudaSetDevice(D.dev));
-    for (int r = 0; r < reps; ++r)
-        if (step(ctx, D, D.fs, op, layer)) return -1;
+    const ffwd_config_t &c = ctx->cfg;
+    Workspace &w = D.ws;
+    for (int r = 0; r < reps; ++r) {
+        if (op == kOpEmbed) {
+            if (embed_step(ctx, D, D.fs, w)) return -1;
+        } else if (op == kOpPool) {
+            LAUNCH(pool_launch(w.x, w.offsets, D.fs.B, c.hidden_size, c.pooling_mode,
+                               c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm,
+                               c.rms_norm_eps, c.normalize_embeddings, w.pooled, w.err, D.stream));
+        } else if (step(ctx, D, D.fs, op, layer)) {
+            return -1;
+        }
+    }
+    return 0;
+}
+
+FFWD_B200_API int ffwd_b200_shard_stats(const ffwd_b200_ctx_t *ctx, int *seqs,
+                                        long long *tokens, double *ms, int cap) {
+    if (!ctx) return -1;
+    const int n = (int)ctx->last_shards.size();
+    for (int i = 0; i < n && i < cap; ++i) {
+        if (seqs) seqs[i] = ctx->last_shards[i].seqs;
+        if (tokens) tokens[i] = ctx->last_shards[i].tokens;
+        if (ms) ms[i] = ctx->last_shards[i].ms;
+    }
+    return n;
+}
+
+FFWD_B200_API int ffwd_b200_test_inject(int kind, int value) {
+    switch (kind) {
+    case FFWD_B200_INJECT_NONE:
+        g_inject_shard.store(-1);
+        g_inject_alloc.store(0);
+        return 0;
+    case FFWD_B200_INJECT_SHARD:
+        g_inject_shard.store(value);
+        return 0;
+    case FFWD_B200_INJECT_ALLOC:
+        g_inject_alloc.store(value < 0 ? 0 : value);
+        return 0;
+    }
+    return -1;
+}
+
+FFWD_B200_API int ffwd_b200_selftest_wait(int device, int limit_us) {
+    t_err.clear();
+    if (limit_us < 1 || limit_us > 1000000) {
+        fail("limit_us must be in [1, 1000000]");
+        return -1;
+    }
+    CK(cudaSetDevice(device));
+    int *err = nullptr;
+    CK(cudaMalloc(&err, 4));
+    int h = 0;
+    cudaError_t e = cudaMemset(err, 0, 4);
+    if (e == cudaSuccess) {
+        g_launches.fetch_add(1);
+        wait_selftest_kernel<<<1, 32>>>(err, (uint64_t)limit_us * 1000ull);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost);
+    cudaFree(err);
+    CK(e);
+    if (h != 0) {
+        fail("device error %d (%s)", h, h == kErrWaitTimeout ? "device wait timed out" : "unknown");
+        return -1;
+    }
     return 0;
 }
 
@@ -2027,9 +2196,13 @@ constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of g_noalloc_scratch per device ordinal, resolved once per
-// device (with that device current) by the first no-allocation call there.
+// device (with that device current) when a model is loaded there.
 uint8_t *g_noalloc_ptr[kNoAllocMaxDevices] = {};
 std::mutex g_noalloc_mu;
+// Host work list of the no-allocation entry, built under g_noalloc_mu (kept
+// off the caller's stack: 8192 items are 192 KiB, more than many worker
+// threads' stacks hold).
+AttnItem g_noalloc_items[kNoAllocMaxItems];
 
 int noalloc_scratch(int dev, uint8_t **out) {
     if (dev < 0 || dev >= kNoAllocMaxDevices) {
@@ -2075,6 +2248,10 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
                                                              const int *h_offsets, int batch,
                                                              float *d_out) {
     t_err.clear();
+    if (h_offsets && batch > 0 && h_offsets[0] != 0) {
+        fail("row offsets must start at 0 (got %d)", h_offsets[0]);
+        return -1;
+    }
     if (!ctx || dev < 0 || dev >= (int)ctx->devs.size() || !d_ids || !h_offsets || batch <= 0 ||
         !d_out) {
         fail("invalid arguments");
@@ -2104,27 +2281,23 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
         return -1;
     }
 
-    // Attention work list, heaviest first (same builder as prepare()).
-    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
-    const bool split = ctx->prec == 2 || ctx->prec == 3;
-    AttnItem items[kNoAllocMaxItems];
-    const int n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
-                                              c.n_heads, c.n_kv_heads, c.head_dim, h_offsets,
-                                              batch, items, kNoAllocMaxItems);
-    if (n_items < 0) {
-        fail("no-allocation encode: more than %d attention work items", kNoAllocMaxItems);
-        return -1;
-    }
-
     // Carve the arena.
     uint8_t *base = nullptr;
     if (noalloc_scratch(D.dev, &base)) return -1;
+    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
+    const bool split = ctx->prec == 2 || ctx->prec == 3;
+    const int n_need = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim,
+                                             h_offsets, batch);
+    if (n_need < 0 || n_need > kNoAllocMaxItems) {
+        fail("no-allocation encode: more than %d attention work items", kNoAllocMaxItems);
+        return -1;
+    }
     const int H = c.hidden_size, I = c.intermediate_size, qkv_dim = c.q_dim + 2 * c.kv_dim;
     Workspace w{};
     Carver cv{base, 0, kNoAllocScratchBytes};
     const size_t ob16 = ctx->prec == 4 ? 2 : 1;  // 16-bit units per GEMM operand element
     bool ok = cv.take(&w.err, 4) && cv.take(&w.offsets, (size_t)batch + 1) &&
-              cv.take(&w.items, (size_t)n_items) && cv.take(&w.ids, (size_t)T) &&
+              cv.take(&w.items, (size_t)n_need) && cv.take(&w.ids, (size_t)T) &&
               cv.take(&w.pos, (size_t)T) && cv.take(&w.x, (size_t)T * H) &&
               cv.take(&w.xb, (size_t)T * H * ob16) && cv.take(&w.att, (size_t)T * c.q_dim * ob16) &&
               cv.take(&w.hmid, (size_t)T * I * ob16);
@@ -2143,57 +2316,30 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     }
     w.cap_t = T;
     w.cap_b = batch + 1;
-    w.cap_items = n_items;
+    w.cap_items = n_need;
 
     cudaStream_t s = D.stream;
+    FwdState fs;
     CK(cudaMemsetAsync(w.err, 0, 16, s));  // error word and scheduler counters
     CK(cudaMemcpyAsync(w.ids, d_ids, (size_t)T * 4, cudaMemcpyDeviceToDevice, s));
     CK(cudaMemcpyAsync(w.offsets, h_offsets, (size_t)(batch + 1) * 4, cudaMemcpyHostToDevice, s));
-    CK(cudaMemcpyAsync(w.items, items, (size_t)n_items * sizeof(AttnItem), cudaMemcpyHostToDevice,
-                       s));
+    {
+        // Attention work list, heaviest first (the builder prepare() uses).  The
+        // copy from pageable memory has left the host array when it returns.
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        fs.n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
+                                           c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, batch,
+                                           g_noalloc_items, kNoAllocMaxItems);
+        if (fs.n_items < 0 || fs.n_items > n_need) {
+            fail("no-allocation encode: attention work list overflow");
+            return -1;
+        }
+        CK(cudaMemcpyAsync(w.items, g_noalloc_items, (size_t)fs.n_items * sizeof(AttnItem),
+                           cudaMemcpyHostToDevice, s));
+    }
 
-    // Forward on the arena buffers: same prepare / step sequence as forward().
-    FwdState fs;
-    fs.T = T;
-    fs.B = batch;
-    fs.n_items = n_items;
-    const bool bert = c.family == FFWD_FAMILY_BERT;
-    const float eps = bert ? c.layer_norm_eps : c.rms_norm_eps;
-    if (make_act_maps(ctx, fs, w, T)) return -1;
-    AttnParams &ap = fs.ap;
-    ap.offsets = w.offsets;
-    ap.items = w.items;
-    ap.n_items = n_items;
-    ap.n_heads = c.n_heads;
-    ap.n_kv_heads = c.n_kv_heads;
-    ap.head_dim = c.head_dim;
-    ap.q_col0 = 0;
-    ap.k_col0 = c.q_dim;
-    ap.v_col0 = c.q_dim + c.kv_dim;
-    ap.causal = c.attention_mode == FFWD_ATTENTION_CAUSAL;
-    ap.scale = 1.0f / sqrtf((float)c.head_dim);
-    ap.out = w.att;
-    ap.ldo = c.q_dim;
-    ap.qkv_f32 = static_cast<const float *>(w.qkv);
-    ap.ldq = qkv_dim;
-    ap.out_hi = w.att;
-    ap.out_lo = w.att_lo;
-    ap.err = w.err;
-    ap.sched = w.err + 2;
-    ap.f16 = ctx->f16 ? 1 : 0;
-    ap.out_tf32 = ctx->prec == 4 ? reinterpret_cast<float *>(w.att) : nullptr;
-
-    const RowOut xb_out{w.xb, split ? w.xb_lo : nullptr, ctx->f16 ? 1 : 0,
-                        ctx->prec == 4 ? reinterpret_cast<float *>(w.xb) : nullptr};
-    LAUNCH((positions_kernel<<<batch, 256, 0, s>>>(w.offsets, bert ? c.position_id_offset : 0,
-                                                   w.pos),
-            cudaGetLastError()));
-    if (bert)
-        LAUNCH(embed_ln_launch(w.ids, w.pos, T, D.embed, D.embed_bf16, c.vocab_size, D.pos_table,
-                               D.type0, D.emb_ln_g, D.emb_ln_b, H, eps, w.x, xb_out, w.err, s));
-    else
-        LAUNCH(embed_rms_launch(w.ids, T, D.embed, D.embed_bf16, c.vocab_size, H, w.x,
-                                D.layers[0].in_norm, eps, xb_out, w.err, s));
+    // Forward on the arena buffers: same setup / step sequence as forward().
+    if (setup_forward(ctx, D, fs, w, T, batch)) return -1;
     D.active_ws = &w;
     int rc = 0;
     for (int li = 0; li < c.n_layers && rc == 0; ++li)
@@ -2201,8 +2347,8 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     D.active_ws = nullptr;
     if (rc) return -1;
     LAUNCH(pool_launch(w.x, w.offsets, batch, H, c.pooling_mode,
-                       bert ? nullptr : D.final_norm, c.rms_norm_eps, c.normalize_embeddings, d_out,
-                       w.err, s));
+                       c.family == FFWD_FAMILY_BERT ? nullptr : D.final_norm, c.rms_norm_eps,
+                       c.normalize_embeddings, d_out, w.err, s));
     int h_err = 0;
     CK(cudaMemcpyAsync(&h_err, w.err, 4, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));

@@ -99,9 +99,11 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parit
 }
 
 // Bounded wait on phase `parity`.  `abort` (shared flag) lets a role give up
-// early once another role of the same CTA has already timed out.
+// early once another role of the same CTA has already timed out.  limit_ns:
+// the time limit (the kernels use the default; a self-test passes a short one).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err,
-                                          volatile int *abort) {
+                                          volatile int *abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t t0 = globaltimer();
@@ -111,7 +113,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
         for (int i = 0; i < 128; ++i)
             if (FFWD_B200_SPIN_PROBE(a, parity)) return true;
         if (abort && *abort) return false;
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit_ns) {
             set_error(err, kErrWaitTimeout);
             if (abort) *abort = 1;
             return false;

@@ -87,6 +87,10 @@ ABI = {
                                                        ctypes.c_void_p, ctypes.c_void_p,
                                                        ctypes.c_int, ctypes.c_void_p]),
     "ffwd_b200_stream": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int]),
+    "ffwd_b200_shard_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_int]),
+    "ffwd_b200_test_inject": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
+    "ffwd_b200_selftest_wait": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "ffwd_b200_run_op": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int]),
     "ffwd_b200_launch_count": (ctypes.c_longlong, []),
@@ -139,6 +143,7 @@ API_ABI = {
                                       ctypes.c_char_p, ctypes.c_size_t]),
     "ffwd_l2_normalize": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "ffwd_cosine_similarity": (ctypes.c_float, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
+    "ffwd_b200_api_context": (ctypes.c_void_p, [ctypes.c_void_p]),
 }
 
 _lib = None
@@ -168,6 +173,28 @@ def api():
     if _api is None:
         _api = _bind(API_LIB_PATH, {**ABI, **API_ABI})
     return _api
+
+
+INJECT_NONE, INJECT_SHARD, INJECT_ALLOC = 0, 1, 2
+
+
+def test_inject(kind: int, value: int = 0, library=None) -> int:
+    """Host-side fault injection (ffwd_b200_test_inject) in `library` (default
+    libffwd_b200.so; the API library keeps its own copy of the switches)."""
+    return (library or lib()).ffwd_b200_test_inject(int(kind), int(value))
+
+
+def shard_stats(ctx, library=None):
+    """[(sequences, tokens, host ms)] per device entry of the last encode_batch."""
+    L = library or lib()
+    n = L.ffwd_b200_shard_stats(ctx, None, None, None, 0)
+    if n <= 0:
+        return []
+    seqs = np.zeros(n, np.int32)
+    toks = np.zeros(n, np.int64)
+    ms = np.zeros(n, np.float64)
+    L.ffwd_b200_shard_stats(ctx, seqs.ctypes.data, toks.ctypes.data, ms.ctypes.data, n)
+    return [(int(a), int(b), float(c)) for a, b, c in zip(seqs, toks, ms)]
 
 
 def last_error() -> str:
@@ -451,6 +478,10 @@ class FfwdApi:
 
     def encode_batch_into(self, ins, n, out) -> int:
         return self._a.ffwd_encode_batch(self.e, ins, n, out)
+
+    def shard_stats(self):
+        """Per device entry of the last encode: (sequences, tokens, host ms)."""
+        return shard_stats(self._a.ffwd_b200_api_context(self.e), self._a)
 
     def encode_batch(self, seqs) -> np.ndarray:
         ins, keep = _pack_inputs(seqs)

@@ -242,24 +242,54 @@ FFWD_B200_API int ffwd_b200_encode_device(ffwd_b200_ctx_t *ctx, int dev, const i
  * other allocations, and latency-sensitive callers for whom cudaMalloc /
  * cudaFree (which can synchronise the device) are off limits on the request
  * path.  This entry allocates nothing: its working buffers live in a fixed
- * 32 MiB arena of device memory reserved, on every GPU that loads the library,
- * until the process exits.  Requests whose buffers do not fit the arena (for
- * example more than about 1300 tokens for a Qwen3-0.6B-shaped model), more
- * than 4096 sequences or 8192 attention work items are rejected with -1 and a
- * message.  The first call on a device resolves the arena's device address
- * with that device current; make that first call before any stream capture.
- * All calls share the one arena and it keeps the last call's contents, so
- * calls whose GPU work overlaps (other streams, other host threads) race.
- * Returns after the work has completed. */
+ * 32 MiB arena of device memory, reserved on a GPU when a model is loaded
+ * there (ffwd_b200_load resolves the arena's address with that device
+ * current) and held until the process exits.  Requests whose buffers do not
+ * fit the arena (for example more than about 1300 tokens for a
+ * Qwen3-0.6B-shaped model), more than 4096 sequences or 8192 attention work
+ * items are rejected with -1 and a message; so are row offsets that do not
+ * start at 0.  The attention work list is built in a static host array, so
+ * the call needs only a small host stack.  All calls share the one arena and
+ * it keeps the last call's contents, so calls whose GPU work overlaps (other
+ * streams, other host threads) race.  The call synchronises the context's
+ * stream and reads an error word back before it returns, so it must not be
+ * called while any stream is being captured. */
 FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ctx, int dev, const int *d_ids,
                                                   const int *h_offsets, int batch, float *d_out);
 
 /* Re-issue `reps` launches of one op of layer `layer` on the buffers of the
  * last forward run on device index dev (enqueued, not synchronised), for
  * per-kernel timing: 0 QKV projection, 1 attention, 2 output projection,
- * 3 first norm, 4 FFN up / gate-up, 5 FFN down, 6 second norm.  Ops that
- * accumulate into the residual stream change the buffers' values. */
+ * 3 first norm, 4 FFN up / gate-up, 5 FFN down, 6 second norm; 7 the
+ * embedding (+ first norm) and 8 the pooling (+ final norm, L2) of the whole
+ * forward (layer ignored).  Ops that accumulate into the residual stream
+ * change the buffers' values. */
 FFWD_B200_API int ffwd_b200_run_op(ffwd_b200_ctx_t *ctx, int dev, int op, int layer, int reps);
+
+/* Per device entry of the context, the last ffwd_b200_encode_batch /
+ * _encode_batch_as call's shard: sequences, tokens and the host wall time in
+ * ms of that entry's worker (packing through copied-out rows).  Writes up to
+ * cap entries (any pointer may be NULL); returns the number of entries. */
+FFWD_B200_API int ffwd_b200_shard_stats(const ffwd_b200_ctx_t *ctx, int *seqs, long long *tokens,
+                                        double *ms, int cap);
+
+/* Host-side fault injection for tests (no GPU fault is involved):
+ * FFWD_B200_INJECT_SHARD, value = device entry: the next shard of an encode
+ * call on that entry fails before anything is uploaded or launched;
+ * FFWD_B200_INJECT_ALLOC, value = n: the next n workspace allocations return
+ * cudaErrorMemoryAllocation; FFWD_B200_INJECT_NONE clears both.  Returns 0,
+ * or -1 for an unknown kind. */
+#define FFWD_B200_INJECT_NONE 0
+#define FFWD_B200_INJECT_SHARD 1
+#define FFWD_B200_INJECT_ALLOC 2
+FFWD_B200_API int ffwd_b200_test_inject(int kind, int value);
+
+/* Self-test of the kernels' bounded waits on GPU `device`: one thread waits
+ * on an mbarrier that nothing arrives at, with a limit of limit_us
+ * microseconds (1 .. 1000000).  The wait gives up, the kernel records its
+ * error code and returns; the call then returns -1 with "device wait timed
+ * out" and the context stays usable. */
+FFWD_B200_API int ffwd_b200_selftest_wait(int device, int limit_us);
 
 /* The CUDA stream (cudaStream_t) the context uses on device index dev. */
 FFWD_B200_API void *ffwd_b200_stream(ffwd_b200_ctx_t *ctx, int dev);

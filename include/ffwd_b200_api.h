@@ -56,6 +56,11 @@ FFWD_B200_API float ffwd_cosine_similarity(const float *a, const float *b, int d
 FFWD_B200_API extern int ffwd_verbose;
 #endif /* FFWD_H */
 
+/* No counterpart in the reference: the backend context behind a pooled-model
+ * handle (NULL before ffwd_activate or for a late-interaction model), so a
+ * host can read ffwd_b200_shard_stats for its ffwd_encode_batch calls. */
+FFWD_B200_API ffwd_b200_ctx_t *ffwd_b200_api_context(ffwd_t *e);
+
 #ifdef __cplusplus
 }
 #endif

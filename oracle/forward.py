@@ -319,6 +319,28 @@ class OracleModel:
             out[b] = l2_normalize(emb) if c["normalize"] else emb
         return out
 
+    # forward.c:492-589 (ffwd_pool_spans, ffwd_model_encode_spans_batch): the
+    # packed forward with the decoder's final RMSNorm applied to every row
+    # (apply_final_norm = 1), then per span the f32 mean of its rows, in span
+    # order; no L2 normalisation.
+    def encode_spans_batch(self, docs, spans) -> np.ndarray:
+        c, t = self.cfg, self.t
+        for doc, sp in zip(docs, spans):
+            if len(doc) <= 0 or not sp:
+                raise ValueError("empty document or span list")
+            for a, n in sp:
+                if a < 0 or n <= 0 or a > len(doc) or n > len(doc) - a:
+                    raise ValueError("span outside its document")
+        x, offs = self.hidden_states(docs)
+        if c["family"] != "bert":
+            x = rms_norm(x, t[self.p + "norm.weight"], c["rms_eps"])
+        out = []
+        for b, sp in enumerate(spans):
+            for a, n in sp:
+                rows = x[offs[b] + a:offs[b] + a + n]
+                out.append((np.sum(rows, 0, dtype=F32) * (F32(1.0) / F32(n))).astype(F32))
+        return np.stack(out)
+
 
 # --------------------------------------------------------------------------- late interaction
 

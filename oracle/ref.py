@@ -32,6 +32,8 @@ def lib():
         l.ref_config.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         l.ref_encode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                  ctypes.c_void_p]
+        l.ref_encode_spans.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] + [
+            ctypes.c_void_p] * 4
         l.ref_forward.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
         l.ref_late_load.restype = ctypes.c_void_p
         l.ref_late_load.argtypes = [ctypes.c_char_p]
@@ -71,6 +73,21 @@ class RefModel:
         rc = self.l.ref_encode(self.h, ids.ctypes.data, lens.ctypes.data, len(seqs), out.ctypes.data)
         if rc != 0:
             raise RuntimeError("reference encode failed")
+        return out
+
+    def encode_spans(self, docs, spans) -> np.ndarray:
+        """ffwd_model_encode_spans_batch: docs (id arrays), spans per doc as
+        (start, n_tokens) pairs; one unnormalised mean row per span."""
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(d, np.int32) for d in docs]))
+        lens = np.ascontiguousarray(np.array([len(d) for d in docs], np.int32))
+        ns = np.ascontiguousarray(np.array([len(sp) for sp in spans], np.int32))
+        st = np.ascontiguousarray(np.array([a for sp in spans for a, _ in sp], np.int32))
+        ln = np.ascontiguousarray(np.array([n for sp in spans for _, n in sp], np.int32))
+        out = np.zeros((int(ns.sum()), self.hidden), dtype=np.float32)
+        if self.l.ref_encode_spans(self.h, ids.ctypes.data, lens.ctypes.data, len(docs),
+                                   ns.ctypes.data, st.ctypes.data, ln.ctypes.data,
+                                   out.ctypes.data) != 0:
+            raise RuntimeError("reference encode_spans failed")
         return out
 
     def forward_states(self, ids) -> np.ndarray:

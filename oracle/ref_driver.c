@@ -91,6 +91,42 @@ ref_encode(void *p, const int *ids, const int *lens, int batch, float *out) {
     return rc;
 }
 
+/* Contextual spans (ffwd_model_encode_spans_batch, forward.c:528-589): ids
+ * concatenated with lens[batch]; n_spans[batch] spans per document, their
+ * (start, n_tokens) pairs concatenated in span_start / span_len. */
+__attribute__((visibility("default"))) int
+ref_encode_spans(void *p, const int *ids, const int *lens, int batch, const int *n_spans,
+                 const int *span_start, const int *span_len, float *out) {
+    ref_handle_t *h = p;
+    int total = 0;
+    for (int b = 0; b < batch; b++)
+        total += n_spans[b];
+    ffwd_context_input_t *in = malloc((size_t)batch * sizeof(*in));
+    ffwd_span_t *sp = malloc((size_t)(total > 0 ? total : 1) * sizeof(*sp));
+    if (!in || !sp) {
+        free(in);
+        free(sp);
+        return -1;
+    }
+    size_t off = 0;
+    int si = 0;
+    for (int b = 0; b < batch; b++) {
+        in[b].input.ids = ids + off;
+        in[b].input.n_tokens = lens[b];
+        in[b].spans = sp + si;
+        in[b].n_spans = n_spans[b];
+        for (int s = 0; s < n_spans[b]; s++, si++) {
+            sp[si].start = span_start[si];
+            sp[si].n_tokens = span_len[si];
+        }
+        off += (size_t)(lens[b] > 0 ? lens[b] : 0);
+    }
+    int rc = ffwd_model_encode_spans_batch(h->model, h->ws, in, batch, out);
+    free(in);
+    free(sp);
+    return rc;
+}
+
 /* Final hidden states of one sequence (Qwen: after the final RMSNorm). */
 __attribute__((visibility("default"))) int
 ref_forward(void *p, const int *ids, int n, float *out_states) {

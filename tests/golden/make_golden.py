@@ -8,9 +8,12 @@ for it through ``ffwd_model_encode_batch``.  ``late/*.npz`` hold late-interactio
 cases: a query, candidate documents and kept-token lists, with the reference's
 ``ffwd_late_model_encode_tokens`` / ``_encode_docs`` vectors and
 ``ffwd_late_maxsim_batch`` scores (the steps of ``ffwd_rerank``).
+``spans/*.npz`` hold contextual-span cases: documents, (start, n_tokens) spans
+and the reference's ``ffwd_model_encode_spans_batch`` rows.
 
     python tests/golden/make_golden.py [case ...]   (needs oracle/_ref: `make -C oracle`;
-                                                     no names: every case)
+                                                     no names: every case;
+                                                     "spans": the spans cases only)
 """
 
 import dataclasses
@@ -53,6 +56,41 @@ LATE_CASES = {
 }
 
 
+SPANS_CASES = {
+    # name: (small spec key, documents builder, spans per document).  Decoder
+    # models only: the reference CPU spans path runs the decoder forward
+    # (forward_packed_inplace, forward.c:572) and refuses BERT-family models.
+    "qwen3_spans": ("qwen3-2l", lambda: small_batch("qwen3-2l", n=2, max_len=180, seed=4),
+                    lambda docs: [[(0, 10), (5, 50), (len(docs[0]) - 1, 1)],
+                                  [(0, len(docs[1])), (3, 7)]]),
+    "qwen3_f32_spans": ("qwen3-f32-2l",
+                        lambda: small_batch("qwen3-f32-2l", n=3, max_len=150, seed=8),
+                        lambda docs: [[(0, len(docs[0]))], [(1, 1), (0, 20), (20, 40)],
+                                      [(len(docs[2]) - 5, 5)]]),
+}
+
+
+def main_spans(root):
+    os.makedirs(os.path.join(HERE, "spans"), exist_ok=True)
+    for name, (key, mk_docs, mk_spans) in SPANS_CASES.items():
+        s = small_spec(key)
+        d = synth.ensure_model(s, root)
+        docs = [np.asarray(q, np.int32) for q in mk_docs()]
+        spans = mk_spans(docs)
+        ref = RefModel(d, threads=os.cpu_count() or 1)
+        out = ref.encode_spans(docs, spans)
+        ref.close()
+        np.savez_compressed(
+            os.path.join(HERE, "spans", f"{name}.npz"),
+            spec=json.dumps(dataclasses.asdict(s)),
+            ids=np.concatenate(docs), lens=np.array([len(q) for q in docs], np.int32),
+            n_spans=np.array([len(sp) for sp in spans], np.int32),
+            span_start=np.array([a for sp in spans for a, _ in sp], np.int32),
+            span_len=np.array([n for sp in spans for _, n in sp], np.int32),
+            expected=out.astype(np.float32))
+        print(name, out.shape)
+
+
 def late_case(spec, q_len, q_keep, doc_lens, seed):
     rng = np.random.default_rng(seed)
     hi = min(spec.vocab - 1, 151642)
@@ -86,6 +124,9 @@ def main_late(root):
 
 def main(only=()):
     root = tempfile.mkdtemp(prefix="ffwd_golden_")
+    if only == ("spans",):
+        main_spans(root)
+        return
     for name, (key, mk) in CASES.items():
         if only and name not in only:
             continue
@@ -105,6 +146,7 @@ def main(only=()):
         print(name, out.shape)
     if not only:
         main_late(root)
+        main_spans(root)
 
 
 if __name__ == "__main__":

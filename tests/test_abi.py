@@ -111,3 +111,28 @@ def test_load_failure_is_loud(tmp_path):
     L = native.lib()
     assert not L.ffwd_b200_load(str(tmp_path).encode())
     assert "config.json" in native.last_error()
+
+
+def test_device_entries_reject_offsets_not_starting_at_zero():
+    # A nonzero first offset would make the id copy read past the caller's
+    # buffer; both device-resident entries refuse it before touching a GPU.
+    L = native.lib()
+    offs = np.array([3, 10, 20], np.int32)
+    assert L.ffwd_b200_encode_device(None, 0, 1, offs.ctypes.data, 2, 1, 1) == -1
+    assert "row offsets must start at 0" in native.last_error()
+    assert L.ffwd_b200_encode_device_noalloc(None, 0, 1, offs.ctypes.data, 2, 1) == -1
+    assert "row offsets must start at 0" in native.last_error()
+    offs[0] = -4
+    assert L.ffwd_b200_encode_device_noalloc(None, 0, 1, offs.ctypes.data, 2, 1) == -1
+    assert "row offsets must start at 0" in native.last_error()
+
+
+def test_fault_injection_switches():
+    L = native.lib()
+    assert native.test_inject(native.INJECT_SHARD, 1) == 0
+    assert native.test_inject(native.INJECT_ALLOC, 2) == 0
+    assert native.test_inject(native.INJECT_NONE) == 0
+    assert native.test_inject(99) == -1
+    assert L.ffwd_b200_selftest_wait(0, 0) == -1  # limit out of range, no launch
+    assert "limit_us" in native.last_error()
+    assert native.shard_stats(None) == []

@@ -1,0 +1,34 @@
+"""Host-side helpers of bench.py that need no GPU: the parity summary the
+bench line carries and the CPU description of its baseline."""
+
+import numpy as np
+
+import bench
+
+
+def test_parity_rows_gate():
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((3, 64)).astype(np.float32)
+    p = bench.parity_rows(a, a)
+    assert p["ok"] and p["rows"] == 3 and p["max_abs"] == 0.0
+    assert abs(p["min_cos"] - 1.0) < 1e-12
+    b = a.copy()
+    b[1] = -b[1]
+    p = bench.parity_rows(a, b)
+    assert not p["ok"] and p["min_cos"] < 0
+    b = a.copy()
+    b[0, 0] = np.nan
+    assert not bench.parity_rows(b, a)["ok"]
+
+
+def test_cpu_info():
+    info = bench.cpu_info()
+    assert info["nproc"] >= 1 and 1 <= info["physical_cores"] <= info["nproc"]
+
+
+def test_flops_per_token_matches_survey():
+    # Qwen3-0.6B: 880.8 MFLOP/token in the projections (2 x MAC, 28 layers)
+    spec, seqs = bench.workload(0)
+    total, lin, attn = bench.flops_per_token(spec, seqs)
+    assert abs(lin / 1e6 - 880.8) < 0.5
+    assert attn > 0 and abs(total - lin - attn) < 1

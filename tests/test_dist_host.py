@@ -33,6 +33,7 @@ def _rank_main(rank, world, port, q):
         d.init(torch)
         assert d.pg and d.world == world and d.rank == rank
         d.barrier(torch)
+        d.cpu_barrier()  # the host-side wait of the sharder leg
         # rank r encodes 1000 (r + 1) tokens per step in 0.5 + r seconds over 3 steps
         rate, max_s, total = bench.whole_job_rate(d, torch, 1000 * (rank + 1), 3, 0.5 + rank)
         spec, seqs = bench.workload(rank)

@@ -11,7 +11,7 @@ import pytest
 from oracle import forward as of
 from oracle import ref as oref
 
-from golden_util import fixtures, load
+from golden_util import fixtures, load, span_fixtures, load_spans
 from helpers import small_spec, small_batch, cos_rows
 from ffwd_b200 import synth
 
@@ -31,6 +31,28 @@ def test_compiled_reference_reproduces_golden(name, model_root):
     spec, d, seqs, expected = load(name, model_root)
     r = oref.RefModel(d, threads=2)
     out = r.encode_batch(seqs)
+    r.close()
+    assert np.abs(out - expected).max() <= 1e-6
+
+
+@pytest.mark.parametrize("name", span_fixtures())
+def test_oracle_spans_match_reference_golden(name, model_root):
+    # ffwd_model_encode_spans_batch (forward.c:528-589) rows.  Span rows are
+    # unnormalised means of final-norm outputs (|x| ~ 1, not the ~0.03 of an L2
+    # row), so the f32 summation-order gate is 1e-5 here.
+    spec, d, docs, spans, expected = load_spans(name, model_root)
+    out = of.OracleModel(d).encode_spans_batch(docs, spans)
+    assert out.shape == expected.shape
+    assert np.abs(out - expected).max() <= 1e-5, name
+    assert cos_rows(out, expected).min() >= 0.999999
+
+
+@pytest.mark.skipif(not oref.available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("name", span_fixtures())
+def test_compiled_reference_reproduces_spans_golden(name, model_root):
+    spec, d, docs, spans, expected = load_spans(name, model_root)
+    r = oref.RefModel(d, threads=2)
+    out = r.encode_spans(docs, spans)
     r.close()
     assert np.abs(out - expected).max() <= 1e-6
 
