@@ -86,22 +86,24 @@ def test_workspace_allocation_failure(reset_devices, model_root):
     s = small_spec("minilm-2l")
     d = synth.ensure_model(s, model_root)
     seqs = small_batch("minilm-2l", n=4)
-    m = native.B200Model(d, gemm_mode="f32", devices=[0])
-    want = m.encode_batch(seqs)
-    # A larger batch makes the workspace grow; its first allocations fail.
     big = small_batch("minilm-2l", n=32, seed=5)
+    want_big = None
     for n_fail in (1, 3):
+        m = native.B200Model(d, gemm_mode="f32", devices=[0])
+        want = m.encode_batch(seqs)
+        # The larger batch makes the workspace grow; its first allocations fail.
         assert native.test_inject(native.INJECT_ALLOC, n_fail) == 0
         rc, _ = m.try_encode_batch(big)
         assert rc == -1
-        assert "out of memory" in native.last_error() or "memory allocation" in \
-            native.last_error().lower()
+        assert "out of memory" in native.last_error()
         native.test_inject(native.INJECT_NONE)
         # the next call allocates again and computes the right thing
         got_big = m.encode_batch(big)
-        assert np.isfinite(got_big).all()
-    assert np.array_equal(m.encode_batch(seqs), want)
-    m.close()
+        if want_big is None:
+            want_big = got_big
+        assert np.array_equal(got_big, want_big)
+        assert np.array_equal(m.encode_batch(seqs), want)
+        m.close()
 
 
 def test_bounded_wait_expires_and_gpu_stays_usable(model_root):
