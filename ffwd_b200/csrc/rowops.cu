@@ -71,9 +71,22 @@ __device__ __forceinline__ void store8_out(RowOut o, size_t off, const float (&v
     if (o.lo) *reinterpret_cast<uint4 *>(o.lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
+// Kernels below keep a whole row in registers when H <= NC * 256 (NC = 1..4:
+// every hidden size of the BERT family and the 0.6B decoder): lane l holds the
+// 8-element groups at columns l * 8 + k * 256, k < NC, so each row is read
+// once and written once.  NC = 0 is the general path for wider rows, which
+// re-reads the row (from L1 / L2) in each pass.  Per-lane partial sums run
+// over k in increasing order in both forms, then a butterfly over the warp:
+// both give the same bits.
+
+template <int NC>
+__device__ __forceinline__ bool col_ok(int c, int H) {
+    return NC == 0 || c < H;
+}
+
 // ---------------------------------------------------------------- Qwen embed
 
-template <bool BF16>
+template <bool BF16, int NC>
 __global__ void __launch_bounds__(kRowWarps * 32)
     embed_rms_kernel(const int *ids, int T, const void *table, int vocab, int H, float *x,
                      const float *w, float eps, RowOut xn, int *err) {
@@ -87,35 +100,67 @@ __global__ void __launch_bounds__(kRowWarps * 32)
         id = 0;
     }
     float *xr = x + (size_t)row * H;
-    float ss = 0.0f;
-    for (int c = lane * 8; c < H; c += 256) {
-        float v[8];
+    auto gather = [&](int c, float (&v)[8]) {
         if (BF16)
             load8_bf16(static_cast<const __nv_bfloat16 *>(table) + (size_t)id * H + c, v);
         else
             load8_ro_f32(static_cast<const float *>(table) + (size_t)id * H + c, v);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 8; ++i)
             if (bad) v[i] = 0.0f;
-            ss += v[i] * v[i];
-        }
-        store8_f32(xr + c, v);
-    }
-    if (!w) return;
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / (float)H + eps);
-    for (int c = lane * 8; c < H; c += 256) {
-        float v[8], g[8];
-        load8_f32(xr + c, v);
-        load8_ro_f32(w + c, g);
+    };
+    float ss = 0.0f;
+    if constexpr (NC > 0) {
+        float v[NC][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
-        store8_out(xn, (size_t)row * H + c, v);
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane * 8 + k * 256;
+            if (c < H) {
+                gather(c, v[k]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) ss += v[k][i] * v[k][i];
+                store8_f32(xr + c, v[k]);
+            }
+        }
+        if (!w) return;
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)H + eps);
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane * 8 + k * 256;
+            if (c < H) {
+                float g[8];
+                load8_ro_f32(w + c, g);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[k][i] = v[k][i] * inv * g[i];
+                store8_out(xn, (size_t)row * H + c, v[k]);
+            }
+        }
+    } else {
+        for (int c = lane * 8; c < H; c += 256) {
+            float v[8];
+            gather(c, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+            store8_f32(xr + c, v);
+        }
+        if (!w) return;
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)H + eps);
+        for (int c = lane * 8; c < H; c += 256) {
+            float v[8], g[8];
+            load8_f32(xr + c, v);
+            load8_ro_f32(w + c, g);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
+            store8_out(xn, (size_t)row * H + c, v);
+        }
     }
 }
 
 // ---------------------------------------------------------------- RMSNorm
 
+template <int NC>
 __global__ void __launch_bounds__(kRowWarps * 32)
     rmsnorm_kernel(const float *x, int T, int H, const float *w, float eps, RowOut xn) {
     const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
@@ -123,27 +168,95 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     if (row >= T) return;
     const float *xr = x + (size_t)row * H;
     float ss = 0.0f;
-    for (int c = lane * 8; c < H; c += 256) {
-        float v[8];
-        load8_f32(xr + c, v);
+    if constexpr (NC > 0) {
+        float v[NC][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
-    }
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / (float)H + eps);
-    for (int c = lane * 8; c < H; c += 256) {
-        float v[8], g[8];
-        load8_f32(xr + c, v);
-        load8_ro_f32(w + c, g);
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane * 8 + k * 256;
+            if (c < H) {
+                load8_f32(xr + c, v[k]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
-        store8_out(xn, (size_t)row * H + c, v);
+                for (int i = 0; i < 8; ++i) ss += v[k][i] * v[k][i];
+            }
+        }
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)H + eps);
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane * 8 + k * 256;
+            if (c < H) {
+                float g[8];
+                load8_ro_f32(w + c, g);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[k][i] = v[k][i] * inv * g[i];
+                store8_out(xn, (size_t)row * H + c, v[k]);
+            }
+        }
+    } else {
+        for (int c = lane * 8; c < H; c += 256) {
+            float v[8];
+            load8_f32(xr + c, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+        }
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / (float)H + eps);
+        for (int c = lane * 8; c < H; c += 256) {
+            float v[8], g[8];
+            load8_f32(xr + c, v);
+            load8_ro_f32(w + c, g);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * g[i];
+            store8_out(xn, (size_t)row * H + c, v);
+        }
     }
 }
 
 // ---------------------------------------------------------------- LayerNorm
 
-// Two-pass mean / variance as in libffwd/norm.c:107-138.
+// Two-pass mean / variance as in libffwd/norm.c:107-138, over a row held in
+// registers (v[k] = columns lane * 8 + k * 256); writes x and the operand copy.
+template <int NC>
+__device__ __forceinline__ void layernorm_regs(float (&v)[NC][8], float *xr, int H, int lane,
+                                               const float *g, const float *b, float eps,
+                                               RowOut xb, size_t off) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NC; ++k)
+        if (lane * 8 + k * 256 < H) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sum += v[k][i];
+        }
+    const float inv_h = 1.0f / (float)H;
+    const float mean = warp_sum(sum) * inv_h;
+    float var = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NC; ++k)
+        if (lane * 8 + k * 256 < H) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float d = v[k][i] - mean;
+                var += d * d;
+            }
+        }
+    var = warp_sum(var) * inv_h;
+    const float inv_std = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int c = lane * 8 + k * 256;
+        if (c < H) {
+            float gg[8], bb[8];
+            load8_ro_f32(g + c, gg);
+            load8_ro_f32(b + c, bb);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[k][i] = gg[i] * (v[k][i] - mean) * inv_std + bb[i];
+            store8_f32(xr + c, v[k]);
+            store8_out(xb, off + c, v[k]);
+        }
+    }
+}
+
+// The same over a row in global memory (general widths).
 __device__ __forceinline__ void layernorm_row(float *xr, int H, int lane, const float *g,
                                               const float *b, float eps, RowOut xb, size_t off) {
     float sum = 0.0f;
@@ -179,14 +292,27 @@ __device__ __forceinline__ void layernorm_row(float *xr, int H, int lane, const 
     }
 }
 
+template <int NC>
 __global__ void __launch_bounds__(kRowWarps * 32)
     layernorm_kernel(float *x, int T, int H, const float *g, const float *b, float eps, RowOut xb) {
     const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
     if (row >= T) return;
-    layernorm_row(x + (size_t)row * H, H, threadIdx.x & 31, g, b, eps, xb, (size_t)row * H);
+    float *xr = x + (size_t)row * H;
+    if constexpr (NC > 0) {
+        float v[NC][8];
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane * 8 + k * 256;
+            if (c < H) load8_f32(xr + c, v[k]);
+        }
+        layernorm_regs<NC>(v, xr, H, lane, g, b, eps, xb, (size_t)row * H);
+    } else {
+        layernorm_row(xr, H, lane, g, b, eps, xb, (size_t)row * H);
+    }
 }
 
-template <bool BF16>
+template <bool BF16, int NC>
 __global__ void __launch_bounds__(kRowWarps * 32)
     embed_ln_kernel(const int *ids, const int *pos, int T, const void *table, int vocab,
                     const float *pos_table, const float *type0, const float *g, const float *b,
@@ -202,20 +328,34 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     }
     const int ps = pos[row];
     float *xr = x + (size_t)row * H;
-    for (int c = lane * 8; c < H; c += 256) {
-        float v[8], pv[8], tv[8];
+    // Same association as libffwd/forward.c:362-365: (tok + pos) + type.
+    auto gather = [&](int c, float (&v)[8]) {
+        float pv[8], tv[8];
         if (BF16)
             load8_bf16(static_cast<const __nv_bfloat16 *>(table) + (size_t)id * H + c, v);
         else
             load8_ro_f32(static_cast<const float *>(table) + (size_t)id * H + c, v);
         load8_ro_f32(pos_table + (size_t)ps * H + c, pv);
         load8_ro_f32(type0 + c, tv);
-        // Same association as libffwd/forward.c:362-365: (tok + pos) + type.
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = bad ? 0.0f : (v[i] + pv[i]) + tv[i];
-        store8_f32(xr + c, v);
+    };
+    if constexpr (NC > 0) {
+        float v[NC][8];
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane * 8 + k * 256;
+            if (c < H) gather(c, v[k]);
+        }
+        layernorm_regs<NC>(v, xr, H, lane, g, b, eps, xb, (size_t)row * H);
+    } else {
+        for (int c = lane * 8; c < H; c += 256) {
+            float v[8];
+            gather(c, v);
+            store8_f32(xr + c, v);
+        }
+        layernorm_row(xr, H, lane, g, b, eps, xb, (size_t)row * H);
     }
-    layernorm_row(xr, H, lane, g, b, eps, xb, (size_t)row * H);
 }
 
 // ---------------------------------------------------------------- pooling
@@ -293,6 +433,80 @@ __global__ void __launch_bounds__(kPoolThreads)
     }
 }
 
+// Mean pooling without a per-row norm (the BERT family): a CTA per sequence
+// whose threads are (row phase, 16-byte column) pairs, so a CTA keeps many
+// row loads in flight; each thread sums the rows of its phase in order, four
+// at a time, then the phases are added in order.  Deterministic: the same
+// batch gives the same bits.
+constexpr int kMeanThreads = 1024;
+
+__global__ void __launch_bounds__(kMeanThreads)
+    pool_mean_kernel(const float *x, const int *starts, const int *ends, int H, int normalize,
+                     float *out, int *err) {
+    __shared__ float4 part[kMeanThreads];
+    __shared__ float red[kMeanThreads / 32];
+    __shared__ float inv_sh;
+    const int b = blockIdx.x;
+    const int s = starts[b], e = ends[b];
+    const int cols = H / 4;
+    const int phases = kMeanThreads / cols;
+    const int t = threadIdx.x;
+    const int ph = t / cols, c4 = t - ph * cols;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    auto add = [](float4 &a, const float4 v) {
+        a.x += v.x;
+        a.y += v.y;
+        a.z += v.z;
+        a.w += v.w;
+    };
+    if (ph < phases) {
+        const float4 *xp = reinterpret_cast<const float4 *>(x) + c4;
+        int r = s + ph;
+        for (; r + 3 * phases < e; r += 4 * phases) {
+            const float4 v0 = xp[(size_t)r * cols];
+            const float4 v1 = xp[(size_t)(r + phases) * cols];
+            const float4 v2 = xp[(size_t)(r + 2 * phases) * cols];
+            const float4 v3 = xp[(size_t)(r + 3 * phases) * cols];
+            add(acc, v0);
+            add(acc, v1);
+            add(acc, v2);
+            add(acc, v3);
+        }
+        for (; r < e; r += phases) add(acc, xp[(size_t)r * cols]);
+    }
+    part[t] = acc;
+    __syncthreads();
+    float4 m = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float ss = 0.0f;
+    if (t < cols) {
+        for (int q = 0; q < phases; ++q) add(m, part[q * cols + t]);
+        const float inv_len = 1.0f / (float)(e - s);
+        m.x *= inv_len;
+        m.y *= inv_len;
+        m.z *= inv_len;
+        m.w *= inv_len;
+        ss = m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
+    }
+    if (normalize) {
+        ss = warp_sum(ss);
+        if ((t & 31) == 0) red[t >> 5] = ss;
+        __syncthreads();
+        if (t == 0) {
+            float tot = 0.0f;
+            for (int w = 0; w < kMeanThreads / 32; ++w) tot += red[w];
+            inv_sh = (tot > 0.0f && isfinite(tot)) ? 1.0f / sqrtf(tot) : 0.0f;
+            if (inv_sh == 0.0f) set_error(err, kErrBadNorm);
+        }
+        __syncthreads();
+        if (inv_sh == 0.0f) return;
+        m.x *= inv_sh;
+        m.y *= inv_sh;
+        m.z *= inv_sh;
+        m.w *= inv_sh;
+    }
+    if (t < cols) reinterpret_cast<float4 *>(out + (size_t)b * H)[t] = m;
+}
+
 constexpr int kEncThreads = 128;
 
 // One CTA per pooled row.
@@ -348,15 +562,31 @@ inline int row_blocks(int T) { return (T + kRowWarps - 1) / kRowWarps; }
 
 }  // namespace
 
+// Registers per row: NC 8-element groups per lane cover H <= NC * 256; 0 for
+// wider rows (the re-reading path).
+inline int row_groups(int H) { return H <= 256 ? 1 : H <= 512 ? 2 : H <= 768 ? 3 : H <= 1024 ? 4 : 0; }
+
+#define FFWD_ROW_DISPATCH(H, KERNEL_NC)       \
+    switch (row_groups(H)) {                  \
+    case 1: KERNEL_NC(1); break;              \
+    case 2: KERNEL_NC(2); break;              \
+    case 3: KERNEL_NC(3); break;              \
+    case 4: KERNEL_NC(4); break;              \
+    default: KERNEL_NC(0); break;             \
+    }
+
 int embed_rms_launch(const int *ids, int T, const void *table, int table_bf16, int vocab, int H,
                      float *x, const float *w, float eps, RowOut xn, int *err, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    if (table_bf16)
-        embed_rms_kernel<true><<<row_blocks(T), kRowWarps * 32, 0, s>>>(ids, T, table, vocab, H, x,
-                                                                       w, eps, xn, err);
-    else
-        embed_rms_kernel<false><<<row_blocks(T), kRowWarps * 32, 0, s>>>(ids, T, table, vocab, H, x,
-                                                                        w, eps, xn, err);
+#define K(NC)                                                                                   \
+    if (table_bf16)                                                                             \
+        embed_rms_kernel<true, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(ids, T, table, vocab, \
+                                                                            H, x, w, eps, xn, err); \
+    else                                                                                        \
+        embed_rms_kernel<false, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(                   \
+            ids, T, table, vocab, H, x, w, eps, xn, err)
+    FFWD_ROW_DISPATCH(H, K)
+#undef K
     return cudaGetLastError();
 }
 
@@ -365,26 +595,33 @@ int embed_ln_launch(const int *ids, const int *pos, int T, const void *table, in
                     const float *b, int H, float eps, float *x, RowOut xb, int *err,
                     cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    if (table_bf16)
-        embed_ln_kernel<true><<<row_blocks(T), kRowWarps * 32, 0, s>>>(
-            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err);
-    else
-        embed_ln_kernel<false><<<row_blocks(T), kRowWarps * 32, 0, s>>>(
-            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err);
+#define K(NC)                                                                                \
+    if (table_bf16)                                                                          \
+        embed_ln_kernel<true, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(                  \
+            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err);          \
+    else                                                                                     \
+        embed_ln_kernel<false, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(                 \
+            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err)
+    FFWD_ROW_DISPATCH(H, K)
+#undef K
     return cudaGetLastError();
 }
 
 int rmsnorm_launch(const float *x, int T, int H, const float *w, float eps, RowOut xn,
                    cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, w, eps, xn);
+#define K(NC) rmsnorm_kernel<NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, w, eps, xn)
+    FFWD_ROW_DISPATCH(H, K)
+#undef K
     return cudaGetLastError();
 }
 
 int layernorm_launch(float *x, int T, int H, const float *g, const float *b, float eps,
                      RowOut xb, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    layernorm_kernel<<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, g, b, eps, xb);
+#define K(NC) layernorm_kernel<NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, g, b, eps, xb)
+    FFWD_ROW_DISPATCH(H, K)
+#undef K
     return cudaGetLastError();
 }
 
@@ -393,8 +630,12 @@ int pool_launch(const float *x, const int *offsets, int batch, int H, int mode,
                 cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
     if (H > kPoolThreads * kPoolMaxCols) return cudaErrorInvalidValue;
-    pool_kernel<<<batch, kPoolThreads, 0, s>>>(x, offsets, offsets + 1, H, mode, norm_w, eps,
-                                                normalize, out, err);
+    if (mode == 0 && !norm_w && H % 4 == 0)
+        pool_mean_kernel<<<batch, kMeanThreads, 0, s>>>(x, offsets, offsets + 1, H, normalize, out,
+                                                        err);
+    else
+        pool_kernel<<<batch, kPoolThreads, 0, s>>>(x, offsets, offsets + 1, H, mode, norm_w, eps,
+                                                    normalize, out, err);
     return cudaGetLastError();
 }
 
@@ -411,8 +652,11 @@ int span_pool_launch(const float *x, const int *starts, const int *ends, int n_s
                      const float *norm_w, float eps, float *out, cudaStream_t s) {
     if (n_spans <= 0) return cudaSuccess;
     if (H > kPoolThreads * kPoolMaxCols) return cudaErrorInvalidValue;
-    pool_kernel<<<n_spans, kPoolThreads, 0, s>>>(x, starts, ends, H, 0, norm_w, eps, 0, out,
-                                                  nullptr);
+    if (!norm_w && H % 4 == 0)
+        pool_mean_kernel<<<n_spans, kMeanThreads, 0, s>>>(x, starts, ends, H, 0, out, nullptr);
+    else
+        pool_kernel<<<n_spans, kPoolThreads, 0, s>>>(x, starts, ends, H, 0, norm_w, eps, 0, out,
+                                                      nullptr);
     return cudaGetLastError();
 }
 
