@@ -522,6 +522,14 @@ def run_ours(args, dist):
         else:
             parity = {"ok": False, "error": "oracle/_ref/libffwd_ref.so not built"}
 
+    # ---------------- the reference's own CUDA backend on the same GPU (N = 1):
+    # libffwd/cuda.cu built unmodified for sm_100a (cuBLAS / cuBLASLt GEMMs;
+    # attention through cuDNN SDPA, its default for this shape, and through its
+    # built-in mma.sync flash kernel), in a process of its own.
+    gpu_ref = None
+    if dist.world == 1 and not args.no_gpu_ref:
+        gpu_ref = gpu_reference_arms(d, args, gpu_rows, e2e_value)
+
     # ---------------- the library's own multi-GPU sharder (N > 1): rank 0 encodes
     # all ranks' batches in one ffwd_encode_batch call over devices 0..N-1 while
     # the other ranks wait on a CPU (gloo) barrier, so no collective kernel
@@ -560,6 +568,7 @@ def run_ours(args, dist):
             "step_split": step_split,
             "parity": parity,
             "sharded_e2e": sharded,
+            "gpu_reference": gpu_ref,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "ffwd_encode_batch (libffwd_b200_api.so)"},
             "gpu_launches": launches,
@@ -572,6 +581,49 @@ def run_ours(args, dist):
         sys.stderr.write(f"parity check failed: {parity}\n")
         return 1
     return 0
+
+
+def gpu_reference_arms(d, args, gpu_rows, e2e_value):
+    """Time the reference CUDA backend (oracle/_ref/libffwd_refcuda.so, built by
+    `make -C oracle cuda`) on this rank's batch through ffwd_cuda_encode_batch
+    with host buffers, once per attention route, each in a child process."""
+    import tempfile
+    from oracle import refcuda
+    if not refcuda.available():
+        return {"unavailable": "oracle/_ref/libffwd_refcuda.so not built (make -C oracle cuda)"}
+    arms = {}
+    steps = max(1, min(args.steps, 5))
+    for name, env in (("cudnn_sdpa", {}), ("builtin_flash", {"FFWD_CUDA_SDPA": "0"})):
+        fd, npy = tempfile.mkstemp(suffix=".npy")
+        os.close(fd)
+        try:
+            r = subprocess.run([sys.executable, "-m", "oracle.refcuda", d, str(steps), "2", "1", npy],
+                               cwd=ROOT, env={**os.environ, **env}, capture_output=True,
+                               text=True, timeout=600)
+            lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+            if r.returncode != 0 or not lines:
+                arms[name] = {"error": (r.stderr or r.stdout)[-300:]}
+                continue
+            arm = json.loads(lines[-1])
+            rows = np.load(npy)
+            a = np.asarray(gpu_rows, np.float64)
+            bb = rows.astype(np.float64)
+            cos = (a * bb).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(bb, axis=1))
+            arm["min_cos_vs_ours"] = float(cos.min())
+            arm["ours_e2e_over_this"] = e2e_value / arm["value"]
+            arm["attention_route"] = (
+                "built-in kernels (cuDNN unavailable)" if "using built-in" in r.stderr
+                else "cuDNN SDPA" if name == "cudnn_sdpa" else "attn_stream_tc128 (mma.sync)")
+            arms[name] = arm
+        except subprocess.TimeoutExpired:
+            arms[name] = {"error": "timed out"}
+        finally:
+            if os.path.exists(npy):
+                os.unlink(npy)
+    arms["note"] = ("reference libffwd/cuda.cu + cuda_sdpa.cu unmodified, nvcc 12.9 sm_100a, "
+                    "ffwd_cuda_encode_batch on the same 128 sequences, host ids in / rows out, "
+                    "wall clock of the synchronous call, --gpu-gemm-mode bf16, bf16 weights")
+    return arms
 
 
 def sharded_leg(d, spec, world, args):
@@ -622,6 +674,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-gpu-ref", action="store_true",
+                    help="skip timing the reference CUDA backend (N = 1)")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the multi-GPU sharder leg (N > 1)")
     args = ap.parse_args()
