@@ -517,135 +517,320 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
 }
 
-// ---------------------------------------------------------------- f32 path
+// ---------------------------------------------------------------- split-bf16 path
 
-constexpr int kF32Threads = 128;
-constexpr int kF32Keys = 32;  // keys per shared-memory block
-constexpr int kF32Dims = 32;  // dimensions per thread: D / 32 threads per query
+// Tensor-core attention of the exact plans.  Q, K and V arrive as bf16 hi / lo
+// pairs (x = hi + lo to about 2^-16 relative, written by the QKV projection's
+// epilogue), and each product runs as three bf16 MMAs with f32 accumulation:
+// S = Qh Kh^T + Qh Kl^T + Ql Kh^T and O += Ph Vh + Ph Vl + Pl Vh, the split-bf16
+// scheme of the exact projections.  One CTA per 128-row query block (block b
+// of work item blockIdx.x / 2), 192 threads:
+//   warps 0-3   softmax: one thread per query row reads its 128 scores from
+//               TMEM, masks them, and writes P = exp2(s - m) split into bf16 hi
+//               (columns 0-63 of the score buffer, keys 2c, 2c + 1 in column c)
+//               and lo (columns 64-127); O is rescaled in place when the row
+//               max grows by more than 2^8; at the end it writes O / l.
+//   warp 4      producer: Q hi and lo once, then per key tile K hi, K lo, V hi,
+//               V lo into a ring of shared-memory slots.
+//   warp 5      allocates TMEM (S [0, 128) | O [128, 256)); one lane issues
+//               S(j), then, after the softmax of tile j, PV(j).  S(j + 1) follows
+//               PV(j) in issue order, so it overwrites P(j) only after PV(j) has
+//               read it, and the completion of S(j + 1) implies that of PV(j).
+constexpr int kSplitThreads = 192;
+constexpr int kSplitProducerWarp = 4;
+constexpr int kSplitMmaWarp = 5;
 
-// CUDA-core attention for the exact plans (f32 scores and accumulation).  A
-// CTA takes kF32Threads * 32 / D queries of one head; each query's D
-// dimensions are split over D / 32 adjacent threads, thread `part` owning the
-// float4 chunks part, part + D / 32, ... (the chunks one shared-memory read
-// instruction touches are consecutive: no bank conflicts).  Keys and values pass
-// through shared memory 32 keys at a time; per block every thread computes its
-// 32 partial scores (broadcast float4 reads of K, reduced over the query's
-// threads by shuffles), takes the block maximum and rescales its running sum
-// and accumulator once, then accumulates exp2(s - m) V.  Scores are kept in
-// the log2 domain (scale * log2 e folded in), so each weight is one ex2.
 template <int D>
-__global__ void __launch_bounds__(kF32Threads)
-    attn_f32_kernel(const AttnParams p) {
-    constexpr int TPQ = D / kF32Dims;
-    constexpr int QT = kF32Threads / TPQ;
-    __shared__ __align__(16) float sk[kF32Keys][D];
-    __shared__ __align__(16) float sv[kF32Keys][D];
+struct SplitCfg {
+    using A = AttnCfg<D>;
+    static constexpr int TILE_BYTES = A::TILE_BYTES;
+    static constexpr int OFF_RING = 2 * TILE_BYTES;  // Q hi, Q lo
+    static constexpr int RING0 = (kSmemCap - 1024 - OFF_RING) / TILE_BYTES;
+    static constexpr int RING = RING0 > 8 ? 8 : RING0;
+    static constexpr int SMEM = OFF_RING + RING * TILE_BYTES + 1024;
+    static_assert(RING >= 4, "K/V ring too small");
+};
 
-    const AttnItem item = p.items[blockIdx.x];
-    const int h = blockIdx.y;
+template <int D>
+__global__ void __launch_bounds__(kSplitThreads, 1)
+    attn_split_kernel(const __grid_constant__ CUtensorMap tm_hi,
+                      const __grid_constant__ CUtensorMap tm_lo, const AttnParams p) {
+    using A = AttnCfg<D>;
+    using C = SplitCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t q_full;
+    __shared__ __align__(8) uint64_t ring_full[C::RING], ring_empty[C::RING];
+    __shared__ __align__(8) uint64_t s_full, p_ready, o_full, drain;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    const AttnItem item = p.items[blockIdx.x >> 1];
+    const int b = blockIdx.x & 1;
+    if (b == 1 && item.qt1 < 0) return;  // the item has one block
+    const int qt = b ? item.qt1 : item.qt0;
+    const int h = b ? item.h1 : item.h0;
     const int kvh = h / (p.n_heads / p.n_kv_heads);
     const int seq0 = p.offsets[item.seq];
     const int L = p.offsets[item.seq + 1] - seq0;
-    const int qi = item.qt0 * QT + threadIdx.x / TPQ;
-    const int part = threadIdx.x % TPQ;
-    const bool qvalid = qi < L;
-    const int kend = p.causal ? min(item.qt0 * QT + QT, L) : L;
-    const float sl2 = p.scale * 1.4426950408889634f;
+    const int kend = p.causal ? min(qt * kTile + kTile, L) : L;
+    const int n_kt = (kend + kTile - 1) / kTile;
 
-    float qv[kF32Dims], acc[kF32Dims];
-    {
-        const float4 *qp = reinterpret_cast<const float4 *>(
-            p.qkv_f32 + (size_t)(seq0 + (qvalid ? qi : 0)) * p.ldq + p.q_col0 + h * D);
-#pragma unroll
-        for (int i = 0; i < kF32Dims / 4; ++i) {
-            const float4 v = qp[part + TPQ * i];
-            qv[4 * i] = v.x * sl2;
-            qv[4 * i + 1] = v.y * sl2;
-            qv[4 * i + 2] = v.z * sl2;
-            qv[4 * i + 3] = v.w * sl2;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t *sQ = smem;
+    uint8_t *sRing = smem + C::OFF_RING;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&q_full, 1);
+        for (int i = 0; i < C::RING; ++i) {
+            mbar_init(&ring_full[i], 1);
+            mbar_init(&ring_empty[i], 1);
         }
-#pragma unroll
-        for (int i = 0; i < kF32Dims; ++i) acc[i] = 0.0f;
+        mbar_init(&s_full, 1);
+        mbar_init(&p_ready, 4);
+        mbar_init(&o_full, 1);
+        mbar_init(&drain, 1);
+        abort_sh = 0;
+        fence_barrier_init();
     }
-    float m = -INFINITY, l = 0.0f;
-    for (int k0 = 0; k0 < kend; k0 += kF32Keys) {
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < kF32Keys * D / 4; idx += kF32Threads) {
-            const int kr = idx / (D / 4), d4 = idx % (D / 4);
-            const int key = k0 + kr;
-            float4 kvv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vvv = kvv;
-            if (key < L) {
-                const float *row = p.qkv_f32 + (size_t)(seq0 + key) * p.ldq;
-                kvv = *reinterpret_cast<const float4 *>(row + p.k_col0 + kvh * D + 4 * d4);
-                vvv = *reinterpret_cast<const float4 *>(row + p.v_col0 + kvh * D + 4 * d4);
+    if (warp == kSplitProducerWarp && lane == 0) {
+        tma_prefetch_desc(&tm_hi);
+        tma_prefetch_desc(&tm_lo);
+    }
+    if (warp == kSplitMmaWarp) {
+        tmem_alloc(&tmem_base_sh, 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = tmem_base_sh;
+
+    if (warp == kSplitProducerWarp) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ producer
+            bool ok = true;
+            int e = 0;  // ring entry: tile j's K hi, K lo, V hi, V lo are 4j .. 4j + 3
+            mbar_arrive_expect_tx(&q_full, 2 * C::TILE_BYTES);
+            for (int part = 0; part < 2; ++part)
+                for (int bx = 0; bx < A::NBOX; ++bx)
+                    tma_load_2d(sQ + part * C::TILE_BYTES + bx * A::BOX_BYTES, part ? &tm_lo : &tm_hi,
+                                &q_full, p.q_col0 + h * D + bx * A::BOXC, seq0 + qt * kTile);
+            for (int j = 0; ok && j < n_kt; ++j)
+                for (int t = 0; t < 4; ++t, ++e) {
+                    const int slot = e % C::RING;
+                    if (!mbar_wait(&ring_empty[slot], ((e / C::RING) & 1) ^ 1, p.err, &abort_sh)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&ring_full[slot], C::TILE_BYTES);
+                    const int col = ((t >> 1) ? p.v_col0 : p.k_col0) + kvh * D;
+                    for (int bx = 0; bx < A::NBOX; ++bx)
+                        tma_load_2d(sRing + slot * C::TILE_BYTES + bx * A::BOX_BYTES,
+                                    (t & 1) ? &tm_lo : &tm_hi, &ring_full[slot],
+                                    col + bx * A::BOXC, seq0 + j * kTile);
+                }
+            if (!ok) {  // let loads in flight land before the CTA exits
+                for (int k = e - C::RING < 0 ? 0 : e - C::RING; k < e; ++k)
+                    mbar_wait(&ring_full[k % C::RING], (k / C::RING) & 1, nullptr, nullptr);
+                mbar_wait(&q_full, 0, nullptr, nullptr);
             }
-            reinterpret_cast<float4 *>(sk[kr])[d4] = kvv;
-            reinterpret_cast<float4 *>(sv[kr])[d4] = vvv;
         }
-        __syncthreads();
-        const int nk = min(kF32Keys, kend - k0);
-        float sc[kF32Keys];
-        float bmax = -INFINITY;
+        __syncwarp();
+    } else if (warp == kSplitMmaWarp) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            constexpr uint32_t IDESC_S = idesc_f16(128, kTile, 1, 1, 0, 0);
+            constexpr uint32_t IDESC_O = idesc_f16(128, D, 1, 1, 0, 1);
+            const uint64_t dQh = smem_desc(smem_u32(sQ), 16, A::SBO, A::LAYOUT);
+            const uint64_t dQl = dQh + (uint64_t)(C::TILE_BYTES >> 4);
+            const uint64_t dRingK = smem_desc(smem_u32(sRing), 16, A::SBO, A::LAYOUT);
+            const uint64_t dRingV = smem_desc(smem_u32(sRing), A::BOX_BYTES, A::SBO, A::LAYOUT);
+            auto kk_off = [](int kk) -> uint64_t {  // K-major k-step offset (16-byte units)
+                const int x = kk * 16;
+                return (uint64_t)(((x / A::BOXC) * A::BOX_BYTES + (x % A::BOXC) * 2) >> 4);
+            };
+            auto slot_off = [](int e) -> uint64_t {
+                return (uint64_t)(((e % C::RING) * C::TILE_BYTES) >> 4);
+            };
+            const uint32_t dS = tmem_base, dO = tmem_base + 128;
+            bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh);
+            for (int j = 0; ok && j < n_kt; ++j) {
+                const int e = 4 * j;
+                if (!mbar_wait(&ring_full[e % C::RING], (e / C::RING) & 1, p.err, &abort_sh) ||
+                    !mbar_wait(&ring_full[(e + 1) % C::RING], ((e + 1) / C::RING) & 1, p.err,
+                               &abort_sh)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t dKh = dRingK + slot_off(e), dKl = dRingK + slot_off(e + 1);
 #pragma unroll
-        for (int j = 0; j < kF32Keys; ++j) {
-            const float4 *kr4 = reinterpret_cast<const float4 *>(&sk[j][0]) + part;
-            float d0 = 0.0f, d1 = 0.0f;
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma_f16(dS, dQh + kk_off(kk), dKh + kk_off(kk), IDESC_S, kk != 0);
 #pragma unroll
-            for (int i = 0; i < kF32Dims / 4; i += 2) {
-                const float4 a = kr4[TPQ * i], b = kr4[TPQ * (i + 1)];
-                d0 = fmaf(qv[4 * i], a.x, d0);
-                d1 = fmaf(qv[4 * i + 1], a.y, d1);
-                d0 = fmaf(qv[4 * i + 2], a.z, d0);
-                d1 = fmaf(qv[4 * i + 3], a.w, d1);
-                d0 = fmaf(qv[4 * i + 4], b.x, d0);
-                d1 = fmaf(qv[4 * i + 5], b.y, d1);
-                d0 = fmaf(qv[4 * i + 6], b.z, d0);
-                d1 = fmaf(qv[4 * i + 7], b.w, d1);
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma_f16(dS, dQh + kk_off(kk), dKl + kk_off(kk), IDESC_S, 1);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma_f16(dS, dQl + kk_off(kk), dKh + kk_off(kk), IDESC_S, 1);
+                umma_commit(&s_full);
+                umma_commit(&ring_empty[e % C::RING]);
+                umma_commit(&ring_empty[(e + 1) % C::RING]);
+                if (!mbar_wait(&p_ready, j & 1, p.err, &abort_sh) ||
+                    !mbar_wait(&ring_full[(e + 2) % C::RING], ((e + 2) / C::RING) & 1, p.err,
+                               &abort_sh) ||
+                    !mbar_wait(&ring_full[(e + 3) % C::RING], ((e + 3) / C::RING) & 1, p.err,
+                               &abort_sh)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t dVh = dRingV + slot_off(e + 2), dVl = dRingV + slot_off(e + 3);
+#pragma unroll
+                for (int kk = 0; kk < kTile / 16; ++kk) {
+                    const uint64_t vo = (uint64_t)((kk * 16 * A::ROWB) >> 4);
+                    umma_f16_ts(dO, dS + kk * 8, dVh + vo, IDESC_O, j != 0 || kk != 0);
+                    umma_f16_ts(dO, dS + kk * 8, dVl + vo, IDESC_O, 1);
+                    umma_f16_ts(dO, dS + 64 + kk * 8, dVh + vo, IDESC_O, 1);
+                }
+                umma_commit(&ring_empty[(e + 2) % C::RING]);
+                umma_commit(&ring_empty[(e + 3) % C::RING]);
             }
-            float dot = d0 + d1;
-#pragma unroll
-            for (int o = 1; o < TPQ; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-            const int key = k0 + j;
-            const bool vis = j < nk && (!p.causal || key <= qi);
-            sc[j] = vis ? dot : -INFINITY;
-            bmax = fmaxf(bmax, sc[j]);
+            umma_commit(ok ? &o_full : &drain);
+            if (!ok) mbar_wait(&drain, 0, nullptr, nullptr);
         }
-        const float m_new = fmaxf(m, bmax);
-        if (m_new == -INFINITY) continue;  // nothing visible yet
-        const float corr = ex2_approx(m - m_new);  // 0 on the first visible block
-        m = m_new;
-        l *= corr;
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------------------- softmax
+        const int r = warp * 32 + lane;
+        const int q = qt * kTile + r;
+        const float sl2 = p.scale * 1.4426950408889634f;
+        const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+        const uint32_t tS = tmem_base + lane_off;
+        const uint32_t tO = tmem_base + lane_off + 128;
+        float m_used = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < n_kt; ++j) {
+            if (!mbar_wait(&s_full, j & 1, p.err, &abort_sh)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float s[kTile];
+            tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
+            tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+            tmem_ld32(tS + 64, *reinterpret_cast<float(*)[32]>(&s[64]));
+            tmem_ld32(tS + 96, *reinterpret_cast<float(*)[32]>(&s[96]));
+            tmem_wait_ld();
+            const int k0 = j * kTile;
+            const int vis = p.causal ? min(L - k0, q - k0 + 1) : L - k0;
+            float rmax = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < kF32Dims; ++i) acc[i] *= corr;
+            for (int i = 0; i < kTile; ++i) {
+                s[i] = i < vis ? s[i] * sl2 : -INFINITY;
+                rmax = fmaxf(rmax, s[i]);
+            }
+            const float m_new = fmaxf(m_used, rmax);
+            const bool rescale = j > 0 && __any_sync(0xffffffffu, m_new > m_used + kRescaleLog2);
+            const float m_old = m_used;
+            if (j == 0 || rescale) m_used = m_new;
+            float la = 0.0f, lb = 0.0f;
 #pragma unroll
-        for (int j = 0; j < kF32Keys; ++j) {
-            const float w = ex2_approx(sc[j] - m);
-            l += w;
-            const float4 *vr4 = reinterpret_cast<const float4 *>(&sv[j][0]) + part;
+            for (int half = 0; half < 2; ++half) {
+                uint32_t ph[32], pl[32];
 #pragma unroll
-            for (int i = 0; i < kF32Dims / 4; ++i) {
-                const float4 v = vr4[TPQ * i];
-                acc[4 * i] = fmaf(w, v.x, acc[4 * i]);
-                acc[4 * i + 1] = fmaf(w, v.y, acc[4 * i + 1]);
-                acc[4 * i + 2] = fmaf(w, v.z, acc[4 * i + 2]);
-                acc[4 * i + 3] = fmaf(w, v.w, acc[4 * i + 3]);
+                for (int i = 0; i < 32; ++i) {
+                    const int k = half * 64 + 2 * i;
+                    const float p0 = ex2_approx(s[k] - m_used), p1 = ex2_approx(s[k + 1] - m_used);
+                    la += p0;
+                    lb += p1;
+                    const __nv_bfloat16 h0 = __float2bfloat16_rn(p0), h1 = __float2bfloat16_rn(p1);
+                    __nv_bfloat162 hh(h0, h1);
+                    ph[i] = *reinterpret_cast<uint32_t *>(&hh);
+                    pl[i] = pack_bf16x2(p0 - __bfloat162float(h0), p1 - __bfloat162float(h1));
+                }
+                tmem_st32u(tS + half * 32, ph);
+                tmem_st32u(tS + 64 + half * 32, pl);
+            }
+            tmem_wait_st();
+            if (rescale) {
+                // PV(j - 1) has completed: S(j), whose completion this thread
+                // waited for, was issued after it.  PV(j) waits for p_ready.
+                const float alpha = ex2_approx(m_old - m_used);
+#pragma unroll 1
+                for (int c = 0; c < D / A::CW; ++c) {
+                    if constexpr (A::CW == 32) {
+                        float o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                        tmem_st32(tO + c * 32, o);
+                    } else {
+                        float o[16];
+                        tmem_ld16(tO + c * 16, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) o[i] *= alpha;
+                        tmem_st16(tO + c * 16, o);
+                    }
+                }
+                tmem_wait_st();
+                l *= alpha;
+            }
+            l += la + lb;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_ready);
+        }
+        if (ok && mbar_wait(&o_full, 0, p.err, &abort_sh)) {
+            tc_fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const size_t off = (size_t)(seq0 + q) * p.ldo + h * D;
+#pragma unroll 1
+            for (int c = 0; c < D / A::CW; ++c) {
+                float o[32];
+                if constexpr (A::CW == 32) {
+                    tmem_ld32(tO + c * 32, o);
+                } else {
+                    tmem_ld16(tO + c * 16, *reinterpret_cast<float(*)[16]>(&o[0]));
+                }
+                tmem_wait_ld();
+                if (q < L) {
+#pragma unroll
+                    for (int i = 0; i < A::CW; i += 4) {
+                        float v[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) v[u] = o[i + u] * inv;
+                        const size_t o4 = off + c * A::CW + i;
+                        if (p.out_tf32) {
+                            *reinterpret_cast<float4 *>(p.out_tf32 + o4) =
+                                make_float4(round_tf32(v[0]), round_tf32(v[1]), round_tf32(v[2]),
+                                            round_tf32(v[3]));
+                        } else {
+                            __nv_bfloat16 hi[4], lo[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                hi[u] = __float2bfloat16_rn(v[u]);
+                                lo[u] = __float2bfloat16_rn(v[u] - __bfloat162float(hi[u]));
+                            }
+                            *reinterpret_cast<uint2 *>(p.out_hi + o4) = *reinterpret_cast<uint2 *>(hi);
+                            *reinterpret_cast<uint2 *>(p.out_lo + o4) = *reinterpret_cast<uint2 *>(lo);
+                        }
+                    }
+                }
             }
         }
     }
-    if (!qvalid) return;
-    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-    const size_t off = (size_t)(seq0 + qi) * p.ldo + h * D;
-#pragma unroll
-    for (int i = 0; i < kF32Dims; ++i) {
-        const size_t o = off + 4 * (part + TPQ * (i / 4)) + (i % 4);  // dimension of acc[i]
-        const float v = acc[i] * inv;
-        if (p.out_tf32) {
-            p.out_tf32[o] = round_tf32(v);
-        } else {
-            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-            p.out_hi[o] = hi;
-            p.out_lo[o] = __float2bfloat16_rn(v - __bfloat162float(hi));
-        }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kSplitMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 256);
     }
 }
 
@@ -682,17 +867,25 @@ int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStr
     return cudaGetLastError();
 }
 
-int attention_f32_qtile(int head_dim) { return kF32Threads * kF32Dims / head_dim; }
-
-int attention_f32_launch(const AttnParams &p, cudaStream_t stream) {
+int attention_split_launch(const CUtensorMap *qkv_hi_map, const CUtensorMap *qkv_lo_map,
+                           const AttnParams &p, cudaStream_t stream) {
     if (p.n_items <= 0) return cudaSuccess;
-    dim3 grid(p.n_items, p.n_heads);
+    dim3 grid(2 * p.n_items);
+    cudaError_t e;
+#define ATTN_SPLIT(DD)                                                                     \
+    do {                                                                                   \
+        e = set_smem_once<attn_split_kernel<DD>>(SplitCfg<DD>::SMEM);                      \
+        if (e != cudaSuccess) return e;                                                    \
+        attn_split_kernel<DD><<<grid, kSplitThreads, SplitCfg<DD>::SMEM, stream>>>(         \
+            *qkv_hi_map, *qkv_lo_map, p);                                                  \
+    } while (0)
     switch (p.head_dim) {
-    case 32: attn_f32_kernel<32><<<grid, kF32Threads, 0, stream>>>(p); break;
-    case 64: attn_f32_kernel<64><<<grid, kF32Threads, 0, stream>>>(p); break;
-    case 128: attn_f32_kernel<128><<<grid, kF32Threads, 0, stream>>>(p); break;
+    case 32: ATTN_SPLIT(32); break;
+    case 64: ATTN_SPLIT(64); break;
+    case 128: ATTN_SPLIT(128); break;
     default: return cudaErrorInvalidValue;
     }
+#undef ATTN_SPLIT
     return cudaGetLastError();
 }
 
@@ -702,15 +895,12 @@ int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 }  // namespace
 
-int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, const int *h_offsets,
-                          int batch) {
+int attention_count_items(int n_heads, int n_kv_heads, const int *h_offsets, int batch) {
     const int rep = n_heads / n_kv_heads;
     long long n = 0;
     for (int b = 0; b < batch; ++b) {
         const int L = h_offsets[b + 1] - h_offsets[b];
-        if (!tc) {
-            n += ceil_div(L, attention_f32_qtile(head_dim));
-        } else if (rep >= 2) {  // head pairs of each key/value head
+        if (rep >= 2) {  // head pairs of each key/value head
             n += (long long)ceil_div(L, kTile) * n_kv_heads * ceil_div(rep, 2);
         } else {  // query-tile pairs of each head
             n += (long long)ceil_div(ceil_div(L, kTile), 2) * n_heads;
@@ -719,8 +909,8 @@ int attention_count_items(bool tc, int n_heads, int n_kv_heads, int head_dim, co
     return n > 0x7fffffff ? -1 : (int)n;
 }
 
-int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int head_dim,
-                          const int *h_offsets, int batch, AttnItem *out, int cap) {
+int attention_build_items(int causal, int n_heads, int n_kv_heads, const int *h_offsets,
+                          int batch, AttnItem *out, int cap) {
     const int rep = n_heads / n_kv_heads;
     int n = 0;
     auto push = [&](const AttnItem &it) -> bool {
@@ -728,19 +918,6 @@ int attention_build_items(bool tc, int causal, int n_heads, int n_kv_heads, int 
         out[n++] = it;
         return true;
     };
-    if (!tc) {
-        for (int b = 0; b < batch; ++b) {
-            const int L = h_offsets[b + 1] - h_offsets[b];
-            const int qt = attention_f32_qtile(head_dim);
-            const int nq = ceil_div(L, qt);
-            for (int t = 0; t < nq; ++t)
-                if (!push(AttnItem{b, t, -1, -1, -1, causal ? t + 1 : nq})) return -1;
-        }
-        std::stable_sort(out, out + n, [](const AttnItem &x, const AttnItem &y) {
-            return x.cost > y.cost;
-        });
-        return n;
-    }
     // Sequences longest first; within a sequence the items of one key/value head
     // (or head) stay together, heaviest query tile first, so the CTAs working at
     // the same time read the same keys and values.

@@ -182,7 +182,7 @@ struct Workspace {
 // re-issued for timing).
 struct FwdState {
     int T = 0, B = 0, n_items = 0;
-    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv, m_kv;
+    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv, m_qkv_lo, m_kv;
     AttnParams ap{};
 };
 
@@ -797,12 +797,26 @@ int gemm(Device &D, int prec, bool f16, const CUtensorMap *a, const CUtensorMap 
     return 0;
 }
 
-// Tensor maps over the GEMM operands of one forward (and, on the 16-bit plans,
-// the qkv matrix for the tensor-core attention): 16-bit with 64-column boxes,
+// The exact plans (prec != 0) keep q, k and v as bf16 hi / lo matrices in the
+// qkv buffer (4 bytes per element): hi first, then lo, each [T, qkv_dim].
+__nv_bfloat16 *qkv_hi(const Workspace &w) { return static_cast<__nv_bfloat16 *>(w.qkv); }
+__nv_bfloat16 *qkv_lo(const Workspace &w, int T, int qkv_dim) {
+    return static_cast<__nv_bfloat16 *>(w.qkv) + (size_t)T * qkv_dim;
+}
+
+// Tensor maps over the GEMM operands of one forward and the qkv matrix (or its
+// hi / lo pair) for the tensor-core attention: 16-bit with 64-column boxes,
 // split-bf16 hi + lo, or tf32-rounded f32 with 32-column boxes.
 int make_act_maps(const ffwd_b200_ctx *ctx, FwdState &fs, const Workspace &w, int T) {
     const ffwd_config_t &c = ctx->cfg;
     const int H = c.hidden_size, I = c.intermediate_size, qkv_dim = c.q_dim + 2 * c.kv_dim;
+    const CUtensorMapSwizzle sw =
+        c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    const int hb = std::min(c.head_dim, 64);
+    if (ctx->prec != 0 &&
+        (make_map(&fs.m_qkv, qkv_hi(w), T, qkv_dim, 128, hb, sw) ||
+         make_map(&fs.m_qkv_lo, qkv_lo(w, T, qkv_dim), T, qkv_dim, 128, hb, sw)))
+        return -1;
     if (ctx->prec == 4) {
         auto m32 = [&](CUtensorMap *m, const void *ptr, int cols) {
             return make_map_dt(m, ptr, T, cols, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -823,10 +837,8 @@ int make_act_maps(const ffwd_b200_ctx *ctx, FwdState &fs, const Workspace &w, in
                        make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)
                    ? -1
                    : 0;
-    const CUtensorMapSwizzle sw =
-        c.head_dim == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
-    return make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, std::min(c.head_dim, 64), sw) ||
-                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, std::min(c.head_dim, 64), sw)
+    return make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, hb, sw) ||
+                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, hb, sw)
                ? -1
                : 0;
 }
@@ -859,8 +871,6 @@ int setup_forward(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, Workspace &w, int
     ap.scale = 1.0f / sqrtf((float)c.head_dim);
     ap.out = w.att;
     ap.ldo = c.q_dim;
-    ap.qkv_f32 = static_cast<const float *>(w.qkv);
-    ap.ldq = qkv_dim;
     ap.out_hi = w.att;
     ap.out_lo = w.att_lo;
     ap.err = w.err;
@@ -908,11 +918,10 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
 
     // Attention work list, heaviest first.
     {
-        const int n = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B);
+        const int n = attention_count_items(c.n_heads, c.n_kv_heads, h_offsets, B);
         if (n < 0 || ensure_ws(ctx, D, T, B, n, 0)) return -1;
-        fs.n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
-                                           c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, B,
-                                           w.h_items, w.cap_items);
+        fs.n_items = attention_build_items(c.attention_mode == FFWD_ATTENTION_CAUSAL, c.n_heads,
+                                           c.n_kv_heads, h_offsets, B, w.h_items, w.cap_items);
         if (fs.n_items < 0) {
             fail("attention work list overflow");
             return -1;
@@ -943,9 +952,10 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
     case kOpQKV: {  // QKV projection (+ bias, + QK-norm and RoPE on the decoder)
         GemmParams p{};
         p.M = T;
-        p.out = w.qkv;
+        p.out = exact ? qkv_hi(w) : w.qkv;
+        p.out_lo = exact ? qkv_lo(w, T, qkv_dim) : nullptr;
         p.ldo = qkv_dim;
-        p.out_mode = exact ? kOutF32 : kOutBF16;
+        p.out_mode = exact ? kOutSplit : kOutBF16;
         p.bias = l.b_qkv;
         p.err = w.err;
         if (bert) {
@@ -968,7 +978,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
     }
     case kOpAttn:
         if (exact)
-            LAUNCH(attention_f32_launch(fs.ap, s));
+            LAUNCH(attention_split_launch(&fs.m_qkv, &fs.m_qkv_lo, fs.ap, s));
         else
             LAUNCH(attention_tc_launch(&fs.m_qkv, fs.ap, s));
         return 0;
@@ -1119,8 +1129,7 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
         const int B = (int)(i1 - i0), T = (int)tok;
         offs.assign(1, 0);
         for (size_t i = i0; i < i1; ++i) offs.push_back(offs.back() + inputs[idx[i]].n_tokens);
-        const int n_items = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim,
-                                                  offs.data(), B);
+        const int n_items = attention_count_items(c.n_heads, c.n_kv_heads, offs.data(), B);
         if (n_items < 0) {
             fail("attention work list too large");
             return -1;
@@ -1486,18 +1495,16 @@ FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts
     return 0;
 }
 
-FFWD_B200_API int ffwd_b200_attention_items(int tc, int causal, int n_heads, int n_kv_heads,
-                                            int head_dim, const int *offsets, int batch,
-                                            int *items, int cap) {
+FFWD_B200_API int ffwd_b200_attention_items(int causal, int n_heads, int n_kv_heads,
+                                            const int *offsets, int batch, int *items, int cap) {
     if (batch < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || cap < 0 ||
         (batch > 0 && !offsets) || (cap > 0 && !items))
         return -1;
-    const int n = attention_count_items(tc != 0, n_heads, n_kv_heads, head_dim, offsets, batch);
+    const int n = attention_count_items(n_heads, n_kv_heads, offsets, batch);
     if (n < 0) return -1;
     if (!items) return n;
     std::vector<AttnItem> v(std::max(n, 1));
-    const int got = attention_build_items(tc != 0, causal, n_heads, n_kv_heads, head_dim, offsets,
-                                          batch, v.data(), n);
+    const int got = attention_build_items(causal, n_heads, n_kv_heads, offsets, batch, v.data(), n);
     if (got < 0 || got > cap) return -1;
     for (int i = 0; i < got; ++i) {
         const AttnItem &it = v[i];
@@ -2286,8 +2293,7 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     if (noalloc_scratch(D.dev, &base)) return -1;
     const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
     const bool split = ctx->prec == 2 || ctx->prec == 3;
-    const int n_need = attention_count_items(!exact, c.n_heads, c.n_kv_heads, c.head_dim,
-                                             h_offsets, batch);
+    const int n_need = attention_count_items(c.n_heads, c.n_kv_heads, h_offsets, batch);
     if (n_need < 0 || n_need > kNoAllocMaxItems) {
         fail("no-allocation encode: more than %d attention work items", kNoAllocMaxItems);
         return -1;
@@ -2327,9 +2333,9 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
         // Attention work list, heaviest first (the builder prepare() uses).  The
         // copy from pageable memory has left the host array when it returns.
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        fs.n_items = attention_build_items(!exact, c.attention_mode == FFWD_ATTENTION_CAUSAL,
-                                           c.n_heads, c.n_kv_heads, c.head_dim, h_offsets, batch,
-                                           g_noalloc_items, kNoAllocMaxItems);
+        fs.n_items = attention_build_items(c.attention_mode == FFWD_ATTENTION_CAUSAL, c.n_heads,
+                                           c.n_kv_heads, h_offsets, batch, g_noalloc_items,
+                                           kNoAllocMaxItems);
         if (fs.n_items < 0 || fs.n_items > n_need) {
             fail("no-allocation encode: attention work list overflow");
             return -1;

@@ -308,14 +308,12 @@ FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx);
 FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts, int *part);
 
 /* Attention work list of a packed batch (host; the list the forward builds),
- * exposed for tests.  tc: tensor-core items (pairs of 128-row query blocks
- * sharing a key/value head) or the f32 path's items.  offsets: [batch + 1] row
- * offsets.  Writes up to cap items as 6 ints each (seq, qt0, h0, qt1, h1,
- * key tiles) when items is non-NULL; returns the item count, -1 on bad
- * arguments or when cap is too small. */
-FFWD_B200_API int ffwd_b200_attention_items(int tc, int causal, int n_heads, int n_kv_heads,
-                                            int head_dim, const int *offsets, int batch,
-                                            int *items, int cap);
+ * exposed for tests: pairs of 128-row query blocks sharing a key/value head.
+ * offsets: [batch + 1] row offsets.  Writes up to cap items as 6 ints each
+ * (seq, qt0, h0, qt1, h1, key tiles) when items is non-NULL; returns the item
+ * count, -1 on bad arguments or when cap is too small. */
+FFWD_B200_API int ffwd_b200_attention_items(int causal, int n_heads, int n_kv_heads,
+                                            const int *offsets, int batch, int *items, int cap);
 
 /* Operator-level entry for tests: Y = X W^T with the tcgen05 GEMM on device
  * pointers (bf16 X [M, K], bf16 W [N, K], f32 Y [M, N]) on the stream of

@@ -19,7 +19,7 @@ def tiles(L, t):
 
 
 def check_tc_cover(lens, heads, kv, hd, causal):
-    it = native.attention_items(lens, heads, kv, hd, causal=causal, tc=True)
+    it = native.attention_items(lens, heads, kv, causal=causal)
     seen = collections.Counter()
     for seq, qt0, h0, qt1, h1, cost in it:
         nq = tiles(lens[seq], 128)
@@ -59,7 +59,7 @@ def test_tensor_core_items_cover_once_random(lens, layout, causal):
 def test_tensor_core_item_order():
     """Longest sequence first; within a sequence the items of one key/value
     head are contiguous, heaviest query tile first."""
-    it = native.attention_items(LENS, 16, 8, 128, causal=True, tc=True)
+    it = native.attention_items(LENS, 16, 8, causal=True)
     seq_order = [s for i, s in enumerate(it[:, 0]) if i == 0 or s != it[i - 1, 0]]
     assert len(seq_order) == len(set(seq_order))  # each sequence in one run
     lens = [LENS[s] for s in seq_order]
@@ -74,27 +74,10 @@ def test_tensor_core_item_order():
             assert list(qts) == sorted(qts, reverse=True)
 
 
-@pytest.mark.parametrize("causal", [True, False])
-@pytest.mark.parametrize("hd", [32, 64, 128])
-def test_f32_items(causal, hd):
-    qt_rows = 128 * 32 // hd
-    it = native.attention_items(LENS, 12, 12, hd, causal=causal, tc=False)
-    seen = collections.Counter()
-    for seq, qt0, h0, qt1, h1, cost in it:
-        nq = tiles(LENS[seq], qt_rows)
-        assert 0 <= qt0 < nq and qt1 < 0
-        assert cost == (qt0 + 1 if causal else nq)
-        seen[(seq, qt0)] += 1
-    assert set(seen) == {(s, t) for s, L in enumerate(LENS) for t in range(tiles(L, qt_rows))}
-    assert max(seen.values()) == 1
-    assert list(it[:, 5]) == sorted(it[:, 5], reverse=True)  # heaviest first
-
-
 def test_bad_arguments():
     L = native.lib()
     offs = np.array([0, 4], np.int32)
-    assert L.ffwd_b200_attention_items(1, 1, 12, 5, 64, offs.ctypes.data, 1, None, 0) == -1
+    assert L.ffwd_b200_attention_items(1, 12, 5, offs.ctypes.data, 1, None, 0) == -1
     out = np.zeros((1, 6), np.int32)
     # 16 heads over 8 kv heads, 4 tokens: 8 items do not fit in 1
-    assert L.ffwd_b200_attention_items(1, 1, 16, 8, 128, offs.ctypes.data, 1,
-                                       out.ctypes.data, 1) == -1
+    assert L.ffwd_b200_attention_items(1, 16, 8, offs.ctypes.data, 1, out.ctypes.data, 1) == -1
