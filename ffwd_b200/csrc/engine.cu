@@ -851,7 +851,6 @@ int embed_step(ffwd_b200_ctx *ctx, Device &D, const FwdState &fs, Workspace &w);
 // D.stream before this).
 int setup_forward(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, Workspace &w, int T, int B) {
     const ffwd_config_t &c = ctx->cfg;
-    const int qkv_dim = c.q_dim + 2 * c.kv_dim;
     fs.T = T;
     fs.B = B;
     if (make_act_maps(ctx, fs, w, T)) return -1;
@@ -908,7 +907,6 @@ int embed_step(ffwd_b200_ctx *ctx, Device &D, const FwdState &fs, Workspace &w) 
 int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int *h_offsets) {
     const ffwd_config_t &c = ctx->cfg;
     Workspace &w = D.ws;
-    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
     const bool bert = c.family == FFWD_FAMILY_BERT;
     cudaStream_t s = D.stream;
 
@@ -1095,7 +1093,6 @@ int run_on_device(ffwd_b200_ctx *ctx, Device &D, const ffwd_input_t *inputs,
                   const std::vector<int> &idx, void *out, const OutSpec &os) {
     const ffwd_config_t &c = ctx->cfg;
     const int H = c.hidden_size;
-    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
     CK(cudaSetDevice(D.dev));
     {
         int entry = (int)(&D - ctx->devs.data());
@@ -2291,7 +2288,7 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
     // Carve the arena.
     uint8_t *base = nullptr;
     if (noalloc_scratch(D.dev, &base)) return -1;
-    const bool exact = ctx->prec != 0;  // f32 qkv and CUDA-core attention
+    const bool exact = ctx->prec != 0;  // split-bf16 qkv and attention
     const bool split = ctx->prec == 2 || ctx->prec == 3;
     const int n_need = attention_count_items(c.n_heads, c.n_kv_heads, h_offsets, batch);
     if (n_need < 0 || n_need > kNoAllocMaxItems) {

@@ -174,32 +174,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                 continue;
             }
             const float *nw = is_q ? p.q_norm : p.k_norm;
-            float inv = 1.0f;
-            if (nw) {
-                float ss = 0.0f;
-#pragma unroll 1
-                for (int c = 0; c < hd / 32; ++c) {
-                    float v[32];
-                    tmem_ld32(tbase + h0 + c * 32, v);
-                    tmem_wait_ld();
-                    if (p.bias && valid) add_bias32(v, p.bias, col0 + c * 32);
-                    float2 s2 = make_float2(0.0f, 0.0f);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float2 x = make_float2(v[2 * i], v[2 * i + 1]);
-                        s2 = fma_f32x2(x, x, s2);
-                    }
-                    ss += s2.x + s2.y;
-                }
-                inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
-            }
+            // f16 tables: the first chunk's cos / sin (64 halves) are loaded
+            // before the sum-of-squares pass, later chunks' between the previous
+            // chunk's two stores, so the L2 latency overlaps other work.
+            const uint4 *c8 = reinterpret_cast<const uint4 *>(p.rope_cos_h + (size_t)ps * half);
+            const uint4 *s8 = reinterpret_cast<const uint4 *>(p.rope_sin_h + (size_t)ps * half);
+            uint4 cv[4], sv[4];
             if constexpr (Sink::kHalfRope) {
-                // f16 tables: each chunk's cos / sin (64 halves) are loaded before
-                // its TMEM reads (the first) or between the previous chunk's two
-                // stores, so the L2 latency overlaps other work.
-                const uint4 *c8 = reinterpret_cast<const uint4 *>(p.rope_cos_h + (size_t)ps * half);
-                const uint4 *s8 = reinterpret_cast<const uint4 *>(p.rope_sin_h + (size_t)ps * half);
-                uint4 cv[4], sv[4];
                 if (half >= 32) {
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -207,6 +188,35 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                         sv[i] = __ldg(s8 + i);
                     }
                 }
+            }
+            float inv = 1.0f;
+            if (nw) {
+                // Two 32-column TMEM loads per wait.
+                float2 s2 = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+                for (int c = 0; c < hd / 32; c += 2) {
+                    float v[32], u[32];
+                    tmem_ld32(tbase + h0 + c * 32, v);
+                    tmem_ld32(tbase + h0 + c * 32 + 32, u);
+                    tmem_wait_ld();
+                    if (p.bias && valid) {
+                        add_bias32(v, p.bias, col0 + c * 32);
+                        add_bias32(u, p.bias, col0 + c * 32 + 32);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = make_float2(v[2 * i], v[2 * i + 1]);
+                        s2 = fma_f32x2(x, x, s2);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = make_float2(u[2 * i], u[2 * i + 1]);
+                        s2 = fma_f32x2(x, x, s2);
+                    }
+                }
+                inv = 1.0f / sqrtf((s2.x + s2.y) / (float)hd + p.eps);
+            }
+            if constexpr (Sink::kHalfRope) {
 #pragma unroll 1
                 for (int c = 0; c < half / 32; ++c) {
                     float x1[32], x2[32];
