@@ -446,6 +446,24 @@ def run_ours(args, dist):
     }
     gpu_rows = d_out.cpu().numpy()
 
+    # ---------------- attention by sequence length: uniform-length batches of
+    # about the bench's token count (layer 0 of the same model), CUDA events
+    attn_by_len = {}
+    rng = np.random.default_rng(7)
+    for Lb in (256, 512, 1024, 2048, 8192):
+        nb = max(1, T // Lb)
+        ids_b = torch.from_numpy(rng.integers(0, 151642, size=nb * Lb).astype(np.int32)).to(
+            f"cuda:{dev}")
+        offs_b = (np.arange(nb + 1) * Lb).astype(np.int32)
+        out_b = torch.empty((nb, H), dtype=torch.float32, device=f"cuda:{dev}")
+        m.encode_device(ids_b.data_ptr(), offs_b, out_b.data_ptr(), sync=True)
+        m.run_op(1, layer=0, reps=2)
+        a_ms = timed(lambda: m.run_op(1, layer=0), reps)
+        fl = 4.0 * q * nb * Lb * (Lb + 1) / 2
+        attn_by_len[f"L{Lb}"] = {"ms": round(a_ms, 4), "tflops": round(fl / (a_ms / 1e3) / 1e12, 1),
+                                 "frac_of_peak": round(fl / (a_ms / 1e3) / 1e12 / peak_tflops, 3)}
+    kernel_report["attention_by_length"] = attn_by_len
+
     # ---------------- end to end through the public API (host buffers)
     os.environ["FFWD_B200_DEVICES"] = str(dev)
     m.close()

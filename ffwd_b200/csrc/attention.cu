@@ -525,17 +525,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // S = Qh Kh^T + Qh Kl^T + Ql Kh^T and O += Ph Vh + Ph Vl + Pl Vh, the split-bf16
 // scheme of the exact projections.  One CTA per 128-row query block (block b
 // of work item blockIdx.x / 2), 192 threads:
-//   warps 0-3   softmax: one thread per query row reads its 128 scores from
-//               TMEM, masks them, and writes P = exp2(s - m) split into bf16 hi
-//               (columns 0-63 of the score buffer, keys 2c, 2c + 1 in column c)
-//               and lo (columns 64-127); O is rescaled in place when the row
-//               max grows by more than 2^8; at the end it writes O / l.
-//   warp 4      producer: Q hi and lo once, then per key tile K hi, K lo, V hi,
-//               V lo into a ring of shared-memory slots.
-//   warp 5      allocates TMEM (S [0, 128) | O [128, 256)); one lane issues
-//               S(j), then, after the softmax of tile j, PV(j).  S(j + 1) follows
-//               PV(j) in issue order, so it overwrites P(j) only after PV(j) has
-//               read it, and the completion of S(j + 1) implies that of PV(j).
+//   warps 0-3   softmax: one thread per query row reads its 128 scores of tile
+//               j from TMEM score buffer j % 2, masks them, and writes
+//               P = exp2(s - m) split into bf16 hi (the buffer's columns 0-63,
+//               keys 2c, 2c + 1 in column c) and lo (columns 64-127); O is
+//               rescaled in place when the row max grows by more than 2^8 (after
+//               waiting for PV(j - 1)); at the end it writes O / l.
+//   warp 4      producer: Q hi and lo once, then K(0), K(1), V(0), K(2), V(1),
+//               K(3), ... (each as hi and lo) into a ring of shared-memory
+//               slots: the order the MMAs consume them.
+//   warp 5      allocates TMEM (S0 [0, 128) | S1 [128, 256) | O [256, 256 + D));
+//               one lane issues S(0), S(1), then per tile PV(j) (after the
+//               softmax of tile j) and S(j + 2).  S(j + 2) goes to the buffer
+//               P(j) sits in and follows PV(j) in issue order, so it overwrites
+//               P(j) only after PV(j) has read it; meanwhile S(j + 1) is already
+//               done, so the softmax of tile j + 1 overlaps PV(j) and S(j + 2).
 constexpr int kSplitThreads = 192;
 constexpr int kSplitProducerWarp = 4;
 constexpr int kSplitMmaWarp = 5;
@@ -548,7 +552,7 @@ struct SplitCfg {
     static constexpr int RING0 = (kSmemCap - 1024 - OFF_RING) / TILE_BYTES;
     static constexpr int RING = RING0 > 8 ? 8 : RING0;
     static constexpr int SMEM = OFF_RING + RING * TILE_BYTES + 1024;
-    static_assert(RING >= 4, "K/V ring too small");
+    static_assert(RING >= 5, "K/V ring too small");
 };
 
 template <int D>
@@ -560,7 +564,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t ring_full[C::RING], ring_empty[C::RING];
-    __shared__ __align__(8) uint64_t s_full, p_ready, o_full, drain;
+    __shared__ __align__(8) uint64_t s_full[2], p_ready[2], o_done, o_full, drain;
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
@@ -588,8 +592,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             mbar_init(&ring_full[i], 1);
             mbar_init(&ring_empty[i], 1);
         }
-        mbar_init(&s_full, 1);
-        mbar_init(&p_ready, 4);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(&p_ready[0], 4);  // per score buffer: a fast softmax warp may run a
+        mbar_init(&p_ready[1], 4);  // tile ahead of the others, so one barrier would mix tiles
+        mbar_init(&o_done, 1);
         mbar_init(&o_full, 1);
         mbar_init(&drain, 1);
         abort_sh = 0;
@@ -600,7 +607,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         tma_prefetch_desc(&tm_lo);
     }
     if (warp == kSplitMmaWarp) {
-        tmem_alloc(&tmem_base_sh, 256);
+        tmem_alloc(&tmem_base_sh, 512);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -612,26 +619,35 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         if (lane == 0) {
             // ------------------------------------------------------------ producer
             bool ok = true;
-            int e = 0;  // ring entry: tile j's K hi, K lo, V hi, V lo are 4j .. 4j + 3
+            int e = 0;
             mbar_arrive_expect_tx(&q_full, 2 * C::TILE_BYTES);
             for (int part = 0; part < 2; ++part)
                 for (int bx = 0; bx < A::NBOX; ++bx)
                     tma_load_2d(sQ + part * C::TILE_BYTES + bx * A::BOX_BYTES, part ? &tm_lo : &tm_hi,
                                 &q_full, p.q_col0 + h * D + bx * A::BOXC, seq0 + qt * kTile);
-            for (int j = 0; ok && j < n_kt; ++j)
-                for (int t = 0; t < 4; ++t, ++e) {
+            // One part (hi and lo entries) of K or V of key tile `tile`.
+            auto load_part = [&](bool is_v, int tile) {
+                for (int part = 0; ok && part < 2; ++part, ++e) {
                     const int slot = e % C::RING;
                     if (!mbar_wait(&ring_empty[slot], ((e / C::RING) & 1) ^ 1, p.err, &abort_sh)) {
                         ok = false;
                         break;
                     }
                     mbar_arrive_expect_tx(&ring_full[slot], C::TILE_BYTES);
-                    const int col = ((t >> 1) ? p.v_col0 : p.k_col0) + kvh * D;
+                    const int col = (is_v ? p.v_col0 : p.k_col0) + kvh * D;
                     for (int bx = 0; bx < A::NBOX; ++bx)
                         tma_load_2d(sRing + slot * C::TILE_BYTES + bx * A::BOX_BYTES,
-                                    (t & 1) ? &tm_lo : &tm_hi, &ring_full[slot],
-                                    col + bx * A::BOXC, seq0 + j * kTile);
+                                    part ? &tm_lo : &tm_hi, &ring_full[slot], col + bx * A::BOXC,
+                                    seq0 + tile * kTile);
                 }
+            };
+            // The order the MMA issuer consumes them.
+            load_part(false, 0);
+            if (n_kt > 1) load_part(false, 1);
+            for (int j = 0; ok && j < n_kt; ++j) {
+                load_part(true, j);
+                if (j + 2 < n_kt) load_part(false, j + 2);
+            }
             if (!ok) {  // let loads in flight land before the CTA exits
                 for (int k = e - C::RING < 0 ? 0 : e - C::RING; k < e; ++k)
                     mbar_wait(&ring_full[k % C::RING], (k / C::RING) & 1, nullptr, nullptr);
@@ -655,17 +671,19 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             auto slot_off = [](int e) -> uint64_t {
                 return (uint64_t)(((e % C::RING) * C::TILE_BYTES) >> 4);
             };
-            const uint32_t dS = tmem_base, dO = tmem_base + 128;
+            const uint32_t dO = tmem_base + 256;
+            int e = 0;  // next ring entry
             bool ok = mbar_wait(&q_full, 0, p.err, &abort_sh);
-            for (int j = 0; ok && j < n_kt; ++j) {
-                const int e = 4 * j;
-                if (!mbar_wait(&ring_full[e % C::RING], (e / C::RING) & 1, p.err, &abort_sh) ||
-                    !mbar_wait(&ring_full[(e + 1) % C::RING], ((e + 1) / C::RING) & 1, p.err,
-                               &abort_sh)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+            auto wait_part = [&]() -> bool {
+                ok = ok && mbar_wait(&ring_full[e % C::RING], (e / C::RING) & 1, p.err, &abort_sh) &&
+                     mbar_wait(&ring_full[(e + 1) % C::RING], ((e + 1) / C::RING) & 1, p.err,
+                               &abort_sh);
+                if (ok) tc_fence_after();
+                return ok;
+            };
+            auto issue_s = [&](int j) {  // S(j) into buffer j % 2
+                if (!wait_part()) return;
+                const uint32_t dS = tmem_base + (j & 1) * kTile;
                 const uint64_t dKh = dRingK + slot_off(e), dKl = dRingK + slot_off(e + 1);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
@@ -676,29 +694,37 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
                     umma_f16(dS, dQl + kk_off(kk), dKh + kk_off(kk), IDESC_S, 1);
-                umma_commit(&s_full);
+                umma_commit(&s_full[j & 1]);
                 umma_commit(&ring_empty[e % C::RING]);
                 umma_commit(&ring_empty[(e + 1) % C::RING]);
-                if (!mbar_wait(&p_ready, j & 1, p.err, &abort_sh) ||
-                    !mbar_wait(&ring_full[(e + 2) % C::RING], ((e + 2) / C::RING) & 1, p.err,
-                               &abort_sh) ||
-                    !mbar_wait(&ring_full[(e + 3) % C::RING], ((e + 3) / C::RING) & 1, p.err,
-                               &abort_sh)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint64_t dVh = dRingV + slot_off(e + 2), dVl = dRingV + slot_off(e + 3);
+                e += 2;
+            };
+            auto issue_pv = [&](int j) {  // O += P(j) V(j), P in buffer j % 2
+                ok = ok && mbar_wait(&p_ready[j & 1], (j >> 1) & 1, p.err, &abort_sh);
+                if (!wait_part()) return;
+                const uint32_t tP = tmem_base + (j & 1) * kTile;
+                const uint64_t dVh = dRingV + slot_off(e), dVl = dRingV + slot_off(e + 1);
 #pragma unroll
                 for (int kk = 0; kk < kTile / 16; ++kk) {
                     const uint64_t vo = (uint64_t)((kk * 16 * A::ROWB) >> 4);
-                    umma_f16_ts(dO, dS + kk * 8, dVh + vo, IDESC_O, j != 0 || kk != 0);
-                    umma_f16_ts(dO, dS + kk * 8, dVl + vo, IDESC_O, 1);
-                    umma_f16_ts(dO, dS + 64 + kk * 8, dVh + vo, IDESC_O, 1);
+                    umma_f16_ts(dO, tP + kk * 8, dVh + vo, IDESC_O, j != 0 || kk != 0);
+                    umma_f16_ts(dO, tP + kk * 8, dVl + vo, IDESC_O, 1);
+                    umma_f16_ts(dO, tP + 64 + kk * 8, dVh + vo, IDESC_O, 1);
                 }
-                umma_commit(&ring_empty[(e + 2) % C::RING]);
-                umma_commit(&ring_empty[(e + 3) % C::RING]);
+                umma_commit(&o_done);
+                umma_commit(&ring_empty[e % C::RING]);
+                umma_commit(&ring_empty[(e + 1) % C::RING]);
+                e += 2;
+            };
+            issue_s(0);
+            if (n_kt > 1) issue_s(1);
+            for (int j = 0; ok && j < n_kt; ++j) {
+                issue_pv(j);
+                if (j + 2 < n_kt) issue_s(j + 2);
             }
+            // o_full: every MMA of the block done (the softmax threads consume
+            // o_done phases only when they rescale, so the last phases of o_done
+            // cannot be told apart by parity).
             umma_commit(ok ? &o_full : &drain);
             if (!ok) mbar_wait(&drain, 0, nullptr, nullptr);
         }
@@ -709,12 +735,12 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         const int q = qt * kTile + r;
         const float sl2 = p.scale * 1.4426950408889634f;
         const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-        const uint32_t tS = tmem_base + lane_off;
-        const uint32_t tO = tmem_base + lane_off + 128;
+        const uint32_t tO = tmem_base + lane_off + 256;
         float m_used = -INFINITY, l = 0.0f;
         bool ok = true;
         for (int j = 0; j < n_kt; ++j) {
-            if (!mbar_wait(&s_full, j & 1, p.err, &abort_sh)) {
+            const uint32_t tS = tmem_base + lane_off + (j & 1) * kTile;
+            if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err, &abort_sh)) {
                 ok = false;
                 break;
             }
@@ -757,8 +783,14 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             }
             tmem_wait_st();
             if (rescale) {
-                // PV(j - 1) has completed: S(j), whose completion this thread
-                // waited for, was issued after it.  PV(j) waits for p_ready.
+                // O holds PV(0 .. j - 2) for sure (S(j) was issued after PV(j - 2)),
+                // so o_done is in phase j - 1 or j: its parity names PV(j - 1)
+                // unambiguously.  PV(j) waits for p_ready.
+                if (!mbar_wait(&o_done, (j - 1) & 1, p.err, &abort_sh)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
                 const float alpha = ex2_approx(m_old - m_used);
 #pragma unroll 1
                 for (int c = 0; c < D / A::CW; ++c) {
@@ -784,7 +816,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
             l += la + lb;
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_ready);
+            if (lane == 0) mbar_arrive(&p_ready[j & 1]);
         }
         if (ok && mbar_wait(&o_full, 0, p.err, &abort_sh)) {
             tc_fence_after();
@@ -830,7 +862,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     __syncthreads();
     if (warp == kSplitMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, 256);
+        tmem_dealloc(tmem_base, 512);
     }
 }
 
