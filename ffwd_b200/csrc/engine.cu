@@ -936,7 +936,7 @@ int step(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int op, int li) {
     const ffwd_config_t &c = ctx->cfg;
     Workspace &w = D.active_ws ? *D.active_ws : D.ws;
     const int prec = ctx->prec;
-    const bool exact = prec != 0;  // f32 qkv and CUDA-core attention
+    const bool exact = prec != 0;  // split-bf16 qkv and attention
     const bool split = prec == 2 || prec == 3;
     const int H = c.hidden_size, I = c.intermediate_size, T = fs.T;
     const int qkv_dim = c.q_dim + 2 * c.kv_dim;

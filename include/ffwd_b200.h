@@ -299,7 +299,7 @@ FFWD_B200_API long long ffwd_b200_launch_count(void);
 FFWD_B200_API const char *ffwd_b200_last_error(void);
 /* Precision plan chosen at load: 0 = single-pass bf16, 1 = single-pass f16,
  * 2 = split-bf16 2-pass, 3 = split-bf16 3-pass, 4 = tf32 (kind::tf32 GEMMs over
- * tf32-rounded f32 operands, f32 attention). */
+ * tf32-rounded f32 operands, split-bf16 attention). */
 FFWD_B200_API int ffwd_b200_precision(const ffwd_b200_ctx_t *ctx);
 
 /* Host-side LPT partition used by the sharder: assigns each of n items with

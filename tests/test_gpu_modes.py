@@ -9,7 +9,7 @@ tensor-core operands (kind::f16 with the f16 format) on the decoder in every
 mode, and on BERT in the 16-bit modes.
 
 Precision codes (ffwd_b200_precision): 0 single-pass bf16, 1 single-pass f16,
-2 / 3 split-bf16 2- / 3-pass, 4 tf32 (kind::tf32 GEMMs, f32 attention).
+2 / 3 split-bf16 2- / 3-pass, 4 tf32 (kind::tf32 GEMMs, split-bf16 attention).
 Gates: exact plans max-abs <= 1e-4 and cosine >= 0.99999 per row; the tf32 plan
 cosine >= 0.9999 and max-abs <= 2e-3 (tf32 keeps 11 significant bits, as the
 reference's CUBLAS_COMPUTE_32F_FAST_TF32 does); 16-bit plans cosine >= 0.999
