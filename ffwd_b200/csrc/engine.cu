@@ -129,13 +129,14 @@ int make_map(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols, uint
                        2);
 }
 
-// Destination map of the two-SM GEMM's TMA epilogue (128 rows x 32 columns).
+// Destination map of the two-SM GEMM's TMA epilogue: 128 rows x 64 bytes (32
+// 16-bit or 16 f32 columns), 64-byte swizzle.
 int make_epi_map(CUtensorMap *m, const GemmParams &p) {
     if (p.epi == kEpiResid)
-        return make_map_dt(m, p.resid, p.M, p.ldr, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+        return make_map_dt(m, p.resid, p.M, p.ldr, 128, 16, CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
     if (p.out_mode == kOutF32)
-        return make_map_dt(m, p.out, p.M, p.ldo, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+        return make_map_dt(m, p.out, p.M, p.ldo, 128, 16, CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
     return make_map_dt(m, p.out, p.M, p.ldo, 128, 32, CU_TENSOR_MAP_SWIZZLE_64B,
                        p.out_mode == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
