@@ -138,6 +138,11 @@ int make_epi_map(CUtensorMap *m, const GemmParams &p) {
     if (p.out_mode == kOutF32)
         return make_map_dt(m, p.out, p.M, p.ldo, 128, 16, CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4);
+    if (p.epi == kEpiQKRope)  // whole heads: two 64-column boxes per store
+        return make_map_dt(m, p.out, p.M, p.ldo, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B,
+                           p.out_mode == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           2);
     return make_map_dt(m, p.out, p.M, p.ldo, 128, 32, CU_TENSOR_MAP_SWIZZLE_64B,
                        p.out_mode == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,

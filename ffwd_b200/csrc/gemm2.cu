@@ -34,10 +34,20 @@ constexpr int kThreads = 64 + 128 * kEpiGroups;
 constexpr int A_BYTES = BM * BK * 2;         // this CTA's X rows
 constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int STAGES = 6;
-constexpr int OFF_STAGING = STAGES * STAGE_BYTES;
+// Shared memory per epilogue kind.  The QK-norm / RoPE epilogue writes a whole
+// head (128 rows x 128 16-bit columns = two 64-column boxes, 32 KB) per
+// warpgroup and stores it at once; it is epilogue-bound, so it keeps 4
+// mainloop stages.  The others stage 64-byte row chunks (8 KB, two per
+// warpgroup) and keep 6.
+template <int EPI>
+struct Cfg2 {
+    static constexpr bool HEAD = EPI == kEpiQKRope;
+    static constexpr int STAGES = HEAD ? 4 : 6;
+    static constexpr int OFF_STAGING = STAGES * STAGE_BYTES;
+    static constexpr int GROUP_STAGING = HEAD ? 32768 : 2 * 8192;
+    static constexpr int SMEM = OFF_STAGING + kEpiGroups * GROUP_STAGING + 1024;
+};
 constexpr int STAGING_BYTES = 8192;  // one 128-row x 64-byte chunk
-constexpr int SMEM = OFF_STAGING + kEpiGroups * 2 * STAGING_BYTES + 1024;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // clears the CTA-rank bit: leader's copy
 
@@ -174,6 +184,39 @@ struct TmaSink {
     __device__ __forceinline__ void finish() {
         if (elected) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
+    // Head-at-a-time output (QK-norm / RoPE epilogue): the warpgroup's 128 rows
+    // x 128 columns go to a 32 KB staging area as two 64-column boxes (128-byte
+    // rows, 128-byte swizzle) and leave in two TMA stores, with one pair of
+    // warpgroup barriers per head instead of one per 32 columns.
+    __device__ __forceinline__ void begin_head() {
+        if (elected) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        named_bar(1 + g, 128);
+    }
+    __device__ __forceinline__ void stage32(const float (&v)[32], int, int local) {
+        uint8_t *box = stage + (local >> 6) * 16384;
+        const int j0 = (local & 63) >> 3;  // first 16-byte chunk of the 32 values
+        const bool f16 = p.out_mode == kOutF16;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4 *>(box + r * 128 + (((j0 + c) ^ (r & 7)) * 16)) =
+                make_uint4(pack16x2(v[8 * c], v[8 * c + 1], f16),
+                           pack16x2(v[8 * c + 2], v[8 * c + 3], f16),
+                           pack16x2(v[8 * c + 4], v[8 * c + 5], f16),
+                           pack16x2(v[8 * c + 6], v[8 * c + 7], f16));
+    }
+    __device__ __forceinline__ void commit_head(int col0) {
+        fence_proxy_async_smem();
+        named_bar(1 + g, 128);
+        if (elected) {
+            for (int b = 0; b < p.head_dim / 64; ++b)
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group"
+                    " [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+                    "r"(smem_u32(stage + b * 16384)), "r"(col0 + 64 * b), "r"(y0)
+                    : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+    }
 };
 
 template <int EPI>
@@ -181,6 +224,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmOut, const GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
+    using CF = Cfg2<EPI>;
+    constexpr int STAGES = CF::STAGES;
     __shared__ __align__(8) uint64_t full_bar[STAGES];
     __shared__ __align__(8) uint64_t empty_bar[STAGES];
     __shared__ __align__(8) uint64_t tfull_bar[2];
@@ -315,7 +360,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         const int g = (warp - 2) >> 2;
         const int row = q * 32 + lane;
-        TmaSink sink{p, &tmOut, smem + OFF_STAGING + g * 2 * STAGING_BYTES, row, 0, g,
+        TmaSink sink{p, &tmOut, smem + CF::OFF_STAGING + g * CF::GROUP_STAGING, row, 0, g,
                      ((warp - 2) & 3) == 0 && lane == 0};
         int lt = 0;
         for (int tile = pair; tile < num_tiles; tile += n_pairs, ++lt) {
@@ -350,13 +395,13 @@ template <int EPI>
 int launch2(const CUtensorMap *a, const CUtensorMap *b_half, const CUtensorMap *out,
             const GemmParams &p, int num_sms, cudaStream_t stream) {
     auto kern = gemm2_kernel<EPI>;
-    cudaError_t e = set_smem_once<gemm2_kernel<EPI>>(SMEM);
+    cudaError_t e = set_smem_once<gemm2_kernel<EPI>>(Cfg2<EPI>::SMEM);
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / BN);
     int grid = 2 * tiles;
     const int cap = num_sms & ~1;
     if (grid > cap) grid = cap;
-    kern<<<grid, kThreads, SMEM, stream>>>(*a, *b_half, *out, p);
+    kern<<<grid, kThreads, Cfg2<EPI>::SMEM, stream>>>(*a, *b_half, *out, p);
     return cudaGetLastError();
 }
 

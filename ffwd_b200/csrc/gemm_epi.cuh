@@ -96,6 +96,12 @@ struct DirectSink {
     const GemmParams &p;
     int grow;
     __device__ __forceinline__ void put(const float (&v)[32], int col) { store_row32(p, grow, col, v); }
+    // Head-at-a-time output (the QK-norm / RoPE epilogue): stores go straight out.
+    __device__ __forceinline__ void begin_head() {}
+    __device__ __forceinline__ void stage32(const float (&v)[32], int col0, int local) {
+        store_row32(p, grow, col0 + local, v);
+    }
+    __device__ __forceinline__ void commit_head(int) {}
     __device__ __forceinline__ void add(const float (&v)[32], int col) {
         float4 *r = reinterpret_cast<float4 *>(p.resid + (size_t)grow * p.ldr + col);
 #pragma unroll
@@ -170,6 +176,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
             const int gh = col0 / hd;
             const bool is_q = gh < nq;
             const bool is_k = !is_q && gh < nq + nkv;
+            sink.begin_head();
             if (!is_q && !is_k) {
 #pragma unroll 1
                 for (int c = 0; c < hd / 32; ++c) {
@@ -178,8 +185,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                     tmem_wait_ld();
                     if (!Sink::kAllRows && !valid) continue;
                     if (p.bias) add_bias32(v, p.bias, col0 + c * 32);
-                    sink.put(v, col0 + c * 32);
+                    sink.stage32(v, col0, c * 32);
                 }
+                sink.commit_head(col0);
                 continue;
             }
             const float *nw = is_q ? p.q_norm : p.k_norm;
@@ -270,7 +278,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                             x2[e] = r2.x; x2[e + 1] = r2.y;
                         }
                     }
-                    sink.put(x1, col0 + c * 32);
+                    sink.stage32(x1, col0, c * 32);
                     if (c + 1 < half / 32) {
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
@@ -278,8 +286,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                             sv[i] = __ldg(s8 + (c + 1) * 4 + i);
                         }
                     }
-                    sink.put(x2, col0 + half + c * 32);
+                    sink.stage32(x2, col0, half + c * 32);
                 }
+                sink.commit_head(col0);
                 continue;
             }
             const float *cs = p.rope_cos + (size_t)ps * half;
@@ -321,9 +330,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
                         x2[4 * i + u] = b * cc[u] + a * ss[u];
                     }
                 }
-                sink.put(x1, col0 + c * 32);
-                sink.put(x2, col0 + half + c * 32);
+                sink.stage32(x1, col0, c * 32);
+                sink.stage32(x2, col0, half + c * 32);
             }
+            sink.commit_head(col0);
         }
     }
 }
