@@ -372,20 +372,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const float inv = p_l > 0.0f ? 1.0f / p_l : 0.0f;
             // Read O_b into packed bf16 registers and release it at once (the
             // next item's first PV may start), then write the row with 32-byte
-            // stores (one full sector each).
+            // stores (one full sector each).  All of the row's columns are
+            // loaded before one wait.
             uint32_t pk[D / 2];
+            float o[D];
 #pragma unroll
             for (int c = 0; c < D / C::CW; ++c) {
-                float o[C::CW];
                 if constexpr (C::CW == 32)
-                    tmem_ld32(tO + c * 32, o);
+                    tmem_ld32(tO + c * 32, *reinterpret_cast<float(*)[32]>(&o[c * 32]));
                 else
-                    tmem_ld16(tO + c * 16, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < C::CW / 2; ++i)
-                    pk[c * (C::CW / 2) + i] = pack16x2(o[2 * i] * inv, o[2 * i + 1] * inv, F16);
+                    tmem_ld16(tO + c * 16, *reinterpret_cast<float(*)[16]>(&o[c * 16]));
             }
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < D / 2; ++i) pk[i] = pack16x2(o[2 * i] * inv, o[2 * i + 1] * inv, F16);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&o_free[b]);
