@@ -644,6 +644,77 @@ def gpu_reference_arms(d, args, gpu_rows, e2e_value):
     return arms
 
 
+# --configs: every BASELINE model family on one GPU, ours beside the reference's
+# own CUDA backend.  (config, gemm mode, sequences per call, spec overrides)
+SWEEP = [
+    ("minilm", "f32", None, {}),
+    ("bge-base", "f32", None, {}),
+    ("bge-base-bf16", "bf16", None, {}),
+    ("xlmr-large", "bf16", None, {}),
+    ("qwen3-0.6b", "bf16", None, {}),
+    # Qwen3-Embedding-8B shape at 4 of its 36 layers (writing the full random
+    # model would take minutes per box); a micro-batch of 4 documents x 8192.
+    ("qwen3-8b", "bf16", 4, {"n_layers": 4}),
+]
+
+
+def config_sweep(args):
+    """One JSON line per BASELINE config: tokens/s through ffwd_b200_encode_batch
+    (host ids in, host rows out, wall clock of the synchronous call, the same
+    contract as the reference's ffwd_cuda_encode_batch) and the reference CUDA
+    backend's tokens/s on the same batch in a child process, with the minimum
+    row cosine between the two."""
+    import tempfile
+    from ffwd_b200 import native
+    from oracle import refcuda
+    steps = max(1, args.steps)
+    for name, mode, batch, over in SWEEP:
+        spec = synth.spec(name, **over) if over else synth.CONFIGS[name]
+        d = synth.ensure_model(spec)
+        seqs = synth.token_batch(name, seed=1, batch=batch)
+        tokens = sum(len(q) for q in seqs)
+        m = native.B200Model(d, gemm_mode=mode, devices=[0])
+        for _ in range(2):
+            ours = m.encode_batch(seqs)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            ours = m.encode_batch(seqs)
+        dt = (time.perf_counter() - t0) / steps
+        m.close()
+        line = {"config": spec.name, "gemm_mode": mode, "sequences": len(seqs),
+                "tokens_per_call": tokens, "ours": {"value": tokens / dt, "unit": UNIT,
+                                                    "ms_per_call": 1000.0 * dt}}
+        if refcuda.available():
+            fd, npy = tempfile.mkstemp(suffix=".npy")
+            os.close(fd)
+            try:
+                r = subprocess.run([sys.executable, "-m", "oracle.refcuda", d, str(steps), "2",
+                                    "1", npy, name, mode, str(len(seqs))], cwd=ROOT,
+                                   capture_output=True, text=True, timeout=900)
+                out = [l for l in r.stdout.splitlines() if l.startswith("{")]
+                if r.returncode != 0 or not out:
+                    line["reference_cuda"] = {"error": (r.stderr or r.stdout)[-300:]}
+                else:
+                    ref = json.loads(out[-1])
+                    rows = np.load(npy).astype(np.float64)
+                    a = ours.astype(np.float64)
+                    cos = (a * rows).sum(1) / (np.linalg.norm(a, axis=1) *
+                                               np.linalg.norm(rows, axis=1))
+                    line["reference_cuda"] = {"value": ref["value"], "unit": UNIT,
+                                              "ms_per_call": ref["ms_per_call"]}
+                    line["ours_over_reference_cuda"] = (tokens / dt) / ref["value"]
+                    line["min_cos_vs_reference_cuda"] = float(cos.min())
+            except subprocess.TimeoutExpired:
+                line["reference_cuda"] = {"error": "timed out"}
+            finally:
+                if os.path.exists(npy):
+                    os.unlink(npy)
+        else:
+            line["reference_cuda"] = {"unavailable": "oracle/_ref/libffwd_refcuda.so not built"}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def sharded_leg(d, spec, world, args):
     """ffwd_encode_batch of all ranks' batches (world x 128 sequences) through
     the public API with FFWD_B200_DEVICES=0..world-1: the library's LPT
@@ -696,7 +767,12 @@ def main():
                     help="skip timing the reference CUDA backend (N = 1)")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the multi-GPU sharder leg (N > 1)")
+    ap.add_argument("--configs", action="store_true",
+                    help="instead of the headline: every BASELINE config on GPU 0, beside "
+                         "the reference's own CUDA backend, one JSON line each")
     args = ap.parse_args()
+    if args.configs:
+        return config_sweep(args)
     if args.warmup < 3:
         args.warmup = 3
     dist = Dist()

@@ -75,10 +75,11 @@ class RefCudaModel:
 
 
 def main(argv=None):
-    """python -m oracle.refcuda MODEL_DIR STEPS WARMUP SEED [OUT.npy]: time the
-    reference CUDA backend's ffwd_cuda_encode_batch on the seeded Qwen3 bench
-    batch (host ids in, host rows out, synchronous: the call a server makes)
-    and print one JSON line; the rows of the last call go to OUT.npy."""
+    """python -m oracle.refcuda MODEL_DIR STEPS WARMUP SEED [OUT.npy [CONFIG [MODE [BATCH]]]]:
+    time the reference CUDA backend's ffwd_cuda_encode_batch on a seeded batch
+    of a BASELINE config (default the Qwen3-0.6B bench batch, bf16 GEMMs; host
+    ids in, host rows out, synchronous: the call a server makes) and print one
+    JSON line; the rows of the last call go to OUT.npy."""
     import json
     import sys
     import time
@@ -88,8 +89,11 @@ def main(argv=None):
 
     a = argv if argv is not None else sys.argv[1:]
     model_dir, steps, warmup, seed = a[0], int(a[1]), int(a[2]), int(a[3])
-    seqs = synth.token_batch("qwen3-0.6b", seed=seed)
-    m = RefCudaModel(model_dir, "bf16")
+    config = a[5] if len(a) > 5 else "qwen3-0.6b"
+    mode = a[6] if len(a) > 6 else "bf16"
+    batch = int(a[7]) if len(a) > 7 else None
+    seqs = synth.token_batch(config, seed=seed, batch=batch)
+    m = RefCudaModel(model_dir, mode)
     ins, keep = m.pack(seqs)
     out = np.zeros((len(seqs), m.hidden), np.float32)
     for _ in range(warmup):
@@ -101,7 +105,7 @@ def main(argv=None):
             raise RuntimeError("reference ffwd_cuda_encode_batch failed")
     dt = (time.perf_counter() - t0) / steps
     m.close()
-    if len(a) > 4:
+    if len(a) > 4 and a[4] != "-":
         np.save(a[4], out)
     tokens = sum(len(s) for s in seqs)
     print(json.dumps({"value": tokens / dt, "unit": "tokens/s", "ms_per_call": 1000 * dt,
