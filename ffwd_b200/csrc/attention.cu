@@ -69,18 +69,22 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     return r;
 }
 
-// Item geometry, recomputed by every role from the shared work list.
+// Item geometry, recomputed by every role from the shared work list.  Rows
+// and key tiles count from seq0; L rows (a window: all its sequences' rows).
 struct ItemGeo {
     int seq0, L, kvh, n_kt;
     int qt0, h0, qt1, h1;
-    bool store1;  // block 1 is a real block (else it repeats block 0, unstored)
+    int seq, nseq;  // first sequence; window size (0: not a window)
+    bool store1;    // block 1 is a real block (else it repeats block 0, unstored)
 };
 
 __device__ __forceinline__ ItemGeo item_geo(const AttnParams &p, int idx) {
     const AttnItem it = p.items[idx];
     ItemGeo g;
     g.seq0 = p.offsets[it.seq];
-    g.L = p.offsets[it.seq + 1] - g.seq0;
+    g.L = p.offsets[it.seq + (it.nseq > 0 ? it.nseq : 1)] - g.seq0;
+    g.seq = it.seq;
+    g.nseq = it.nseq;
     g.store1 = it.qt1 >= 0;
     g.qt0 = it.qt0;
     g.h0 = it.h0;
@@ -409,6 +413,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (item_sh[k % kItemSlots] < 0) break;
             const ItemGeo it = geo_sh[k % kItemSlots];
             const int q = (b ? it.qt1 : it.qt0) * kTile + r;
+            // Keys [lo, hi) (rows from seq0) are this row's sequence: the whole
+            // item, or in a window the row's own sequence (none past the window).
+            int lo = 0, hi = it.L;
+            if (it.nseq > 0) {
+                lo = hi = 0;
+                if (q < it.L) {
+                    int a = it.seq, z = it.seq + it.nseq - 1;
+                    while (a < z) {
+                        const int mid = (a + z + 1) >> 1;
+                        if (p.offsets[mid] - it.seq0 <= q)
+                            a = mid;
+                        else
+                            z = mid - 1;
+                    }
+                    lo = p.offsets[a] - it.seq0;
+                    hi = p.offsets[a + 1] - it.seq0;
+                }
+            }
+            if (p.causal) hi = min(hi, q + 1);
             float m_used = -INFINITY, l = 0.0f;
             for (int j = 0; j < it.n_kt; ++j, ++g) {
                 if (!mbar_wait(&s_full[b], g & 1, p.err, &abort_sh)) {
@@ -423,10 +446,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 tmem_ld32(tS + 96, *reinterpret_cast<float(*)[32]>(&s[96]));
                 tmem_wait_ld();
                 const int k0 = j * kTile;
-                const int vis = p.causal ? min(it.L - k0, q - k0 + 1) : it.L - k0;
-                if (vis < kTile) {
+                const int vlo = lo - k0, vhi = hi - k0;  // visible columns of this tile
+                if (vlo > 0 || vhi < kTile) {
 #pragma unroll
-                    for (int i = 0; i < kTile; ++i) s[i] = i < vis ? s[i] : -INFINITY;
+                    for (int i = 0; i < kTile; ++i) s[i] = i >= vlo && i < vhi ? s[i] : -INFINITY;
                 }
                 float mx[4];
 #pragma unroll
@@ -450,7 +473,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 // are bound by instruction issue.  (A packed add for the row sum
                 // was measured to cost registers: it spills.)
                 float2 la[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-                const float2 scale2 = make_float2(sl2, sl2), neg_m2 = make_float2(-m_used, -m_used);
+                // (m_used is -inf only while the row has seen no visible key: then
+                // every score is -inf and 0 keeps P at 0.)
+                const float mu = m_used == -INFINITY ? 0.0f : m_used;
+                const float2 scale2 = make_float2(sl2, sl2), neg_m2 = make_float2(-mu, -mu);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     uint32_t pk[32];
@@ -469,7 +495,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     // PV_b(g - 1) has completed: S_b(g), whose completion this
                     // thread waited for, was issued after it.  PV_b(g) waits for
                     // the s_free arrival below.
-                    const float alpha = ex2_approx(m_old - m_used);
+                    // A row with no visible key before this tile (a window row
+                    // whose sequence starts in a later key tile) holds O = 0, l = 0.
+                    const float alpha = m_old == -INFINITY ? 0.0f : ex2_approx(m_old - m_used);
 #pragma unroll 1
                     for (int c = 0; c < D / C::CW; ++c) {
                         float o[32];
@@ -942,7 +970,7 @@ int attention_count_items(int n_heads, int n_kv_heads, const int *h_offsets, int
 }
 
 int attention_build_items(int causal, int n_heads, int n_kv_heads, const int *h_offsets,
-                          int batch, AttnItem *out, int cap) {
+                          int batch, AttnItem *out, int cap, bool windows) {
     const int rep = n_heads / n_kv_heads;
     int n = 0;
     auto push = [&](const AttnItem &it) -> bool {
@@ -950,6 +978,9 @@ int attention_build_items(int causal, int n_heads, int n_kv_heads, const int *h_
         out[n++] = it;
         return true;
     };
+    auto len = [&](int b) { return h_offsets[b + 1] - h_offsets[b]; };
+    // A sequence goes into a window when it fits one query tile.
+    auto short_seq = [&](int b) { return windows && len(b) > 0 && len(b) <= kTile; };
     // Sequences longest first; within a sequence the items of one key/value head
     // (or head) stay together, heaviest query tile first, so the CTAs working at
     // the same time read the same keys and values.
@@ -959,7 +990,8 @@ int attention_build_items(int causal, int n_heads, int n_kv_heads, const int *h_
         return h_offsets[x + 1] - h_offsets[x] > h_offsets[y + 1] - h_offsets[y];
     });
     for (int b : order) {
-        const int L = h_offsets[b + 1] - h_offsets[b];
+        if (short_seq(b)) continue;
+        const int L = len(b);
         const int nq = ceil_div(L, kTile);
         if (rep >= 2) {
             for (int kvh = 0; kvh < n_kv_heads; ++kvh)
@@ -967,7 +999,7 @@ int attention_build_items(int causal, int n_heads, int n_kv_heads, const int *h_
                     for (int h = kvh * rep; h < (kvh + 1) * rep; h += 2) {
                         const bool pair = h + 1 < (kvh + 1) * rep;
                         if (!push(AttnItem{b, t, h, pair ? t : -1, pair ? h + 1 : -1,
-                                           causal ? t + 1 : nq}))
+                                           causal ? t + 1 : nq, 0}))
                             return -1;
                     }
         } else {
@@ -975,10 +1007,36 @@ int attention_build_items(int causal, int n_heads, int n_kv_heads, const int *h_
                 for (int t = nq - 1; t >= 0; t -= 2) {
                     const bool pair = t >= 1;
                     if (!push(AttnItem{b, pair ? t - 1 : t, h, pair ? t : -1, pair ? h : -1,
-                                       causal ? t + 1 : nq}))
+                                       causal ? t + 1 : nq, 0}))
                         return -1;
                 }
         }
+    }
+    // Windows: runs of neighbouring short sequences, cut at 128 rows (two heads
+    // per item) or 256 rows (the window's two halves per item).
+    const int cap_rows = rep >= 2 ? kTile : 2 * kTile;
+    for (int b = 0; b < batch;) {
+        if (!short_seq(b)) {
+            ++b;
+            continue;
+        }
+        int e = b, rows = 0;
+        while (e < batch && short_seq(e) && rows + len(e) <= cap_rows) rows += len(e++);
+        const int nseq = e - b;
+        const int nt = ceil_div(rows, kTile);
+        if (rep >= 2) {
+            for (int kvh = 0; kvh < n_kv_heads; ++kvh)
+                for (int h = kvh * rep; h < (kvh + 1) * rep; h += 2) {
+                    const bool pair = h + 1 < (kvh + 1) * rep;
+                    if (!push(AttnItem{b, 0, h, pair ? 0 : -1, pair ? h + 1 : -1, 1, nseq}))
+                        return -1;
+                }
+        } else {
+            for (int h = 0; h < n_heads; ++h)
+                if (!push(AttnItem{b, 0, h, nt > 1 ? 1 : -1, nt > 1 ? h : -1, nt, nseq}))
+                    return -1;
+        }
+        b = e;
     }
     return n;
 }

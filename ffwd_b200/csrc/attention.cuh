@@ -18,12 +18,17 @@ namespace fb {
 
 // One work item: two query blocks of 128 rows that share their keys and
 // values, block 0 = (query tile qt0, head h0), block 1 = (qt1, h1); qt1 = h1 =
-// -1 when the item has block 0 only.
+// -1 when the item has block 0 only.  Tiles count from the first row of
+// sequence `seq`.  nseq > 0 makes the item a window over the nseq consecutive
+// short sequences seq .. seq + nseq - 1 (at most 128 rows when the two blocks
+// are two heads, 256 when they are the window's two 128-row halves): its keys
+// are the window's rows and each query row sees only its own sequence.
 struct AttnItem {
     int seq;
     int qt0, h0;
     int qt1, h1;
-    int cost;  // key tiles x blocks, for heaviest-first ordering
+    int cost;  // key tiles, for heaviest-first ordering
+    int nseq;  // 0: one sequence; > 0: window of nseq short sequences
 };
 
 struct AttnParams {
@@ -50,12 +55,16 @@ struct AttnParams {
 // Build the work list of a packed batch (host): pairs of 128-row query blocks
 // sharing a key/value head (two query heads of a group, or two adjacent query
 // tiles when every head has its own key/value head), ordered longest sequence
-// first with the items of one key/value head together.  Writes at most cap
-// items to out; returns the count, or -1 if cap is too small.  Allocates
-// nothing beyond a sequence order of `batch` ints.
+// first with the items of one key/value head together.  With `windows`,
+// sequences of at most 128 rows that are neighbours in the packed layout share
+// items (windows, see AttnItem), placed after the rest; only the 16-bit
+// kernel reads windows.  Writes at most cap items to out; returns the count,
+// or -1 if cap is too small.  Allocates nothing beyond a sequence order of
+// `batch` ints.
 int attention_build_items(int causal, int n_heads, int n_kv_heads, const int *h_offsets,
-                          int batch, AttnItem *out, int cap);
-// Number of items attention_build_items would write.
+                          int batch, AttnItem *out, int cap, bool windows = false);
+// Number of items attention_build_items would write without windows (an upper
+// bound with them).
 int attention_count_items(int n_heads, int n_kv_heads, const int *h_offsets, int batch);
 
 // 16-bit plans.  `qkv_map`: 2-D 16-bit map over the qkv matrix with a box of

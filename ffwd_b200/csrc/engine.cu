@@ -925,7 +925,8 @@ int prepare(ffwd_b200_ctx *ctx, Device &D, FwdState &fs, int T, int B, const int
         const int n = attention_count_items(c.n_heads, c.n_kv_heads, h_offsets, B);
         if (n < 0 || ensure_ws(ctx, D, T, B, n, 0)) return -1;
         fs.n_items = attention_build_items(c.attention_mode == FFWD_ATTENTION_CAUSAL, c.n_heads,
-                                           c.n_kv_heads, h_offsets, B, w.h_items, w.cap_items);
+                                           c.n_kv_heads, h_offsets, B, w.h_items, w.cap_items,
+                                           ctx->prec == 0);
         if (fs.n_items < 0) {
             fail("attention work list overflow");
             return -1;
@@ -1498,7 +1499,7 @@ FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts
     return 0;
 }
 
-FFWD_B200_API int ffwd_b200_attention_items(int causal, int n_heads, int n_kv_heads,
+FFWD_B200_API int ffwd_b200_attention_items(int causal, int windows, int n_heads, int n_kv_heads,
                                             const int *offsets, int batch, int *items, int cap) {
     if (batch < 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || cap < 0 ||
         (batch > 0 && !offsets) || (cap > 0 && !items))
@@ -1507,17 +1508,19 @@ FFWD_B200_API int ffwd_b200_attention_items(int causal, int n_heads, int n_kv_he
     if (n < 0) return -1;
     if (!items) return n;
     std::vector<AttnItem> v(std::max(n, 1));
-    const int got = attention_build_items(causal, n_heads, n_kv_heads, offsets, batch, v.data(), n);
+    const int got = attention_build_items(causal, n_heads, n_kv_heads, offsets, batch, v.data(), n,
+                                          windows != 0);
     if (got < 0 || got > cap) return -1;
     for (int i = 0; i < got; ++i) {
         const AttnItem &it = v[i];
-        int *o = items + 6 * i;
+        int *o = items + 7 * i;
         o[0] = it.seq;
         o[1] = it.qt0;
         o[2] = it.h0;
         o[3] = it.qt1;
         o[4] = it.h1;
         o[5] = it.cost;
+        o[6] = it.nseq;
     }
     return got;
 }
@@ -2338,7 +2341,7 @@ extern "C" FFWD_B200_API int ffwd_b200_encode_device_noalloc(ffwd_b200_ctx_t *ct
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
         fs.n_items = attention_build_items(c.attention_mode == FFWD_ATTENTION_CAUSAL, c.n_heads,
                                            c.n_kv_heads, h_offsets, batch, g_noalloc_items,
-                                           kNoAllocMaxItems);
+                                           kNoAllocMaxItems, ctx->prec == 0);
         if (fs.n_items < 0 || fs.n_items > n_need) {
             fail("no-allocation encode: attention work list overflow");
             return -1;

@@ -99,8 +99,8 @@ ABI = {
     "ffwd_b200_lpt_partition": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                                ctypes.c_void_p]),
     "ffwd_b200_attention_items": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                                 ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
-                                                 ctypes.c_int]),
+                                                 ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                                 ctypes.c_void_p, ctypes.c_int]),
     "ffwd_b200_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                            ctypes.c_int, ctypes.c_int, ctypes.c_int]),
@@ -415,21 +415,22 @@ def lpt_partition(costs, n_parts: int) -> np.ndarray:
     return part
 
 
-def attention_items(lens, n_heads, n_kv_heads, causal=True) -> np.ndarray:
+def attention_items(lens, n_heads, n_kv_heads, causal=True, windows=False) -> np.ndarray:
     """The forward's attention work list for sequences of these lengths:
-    [n, 6] int32 rows (seq, qt0, h0, qt1, h1, key tiles)."""
+    [n, 7] int32 rows (seq, qt0, h0, qt1, h1, key tiles, window sequences).
+    windows=True: the 16-bit plans' list, short neighbours sharing items."""
     offs = np.ascontiguousarray(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32))
     L = lib()
-    n = L.ffwd_b200_attention_items(int(causal), n_heads, n_kv_heads, offs.ctypes.data,
-                                    len(lens), None, 0)
+    n = L.ffwd_b200_attention_items(int(causal), int(windows), n_heads, n_kv_heads,
+                                    offs.ctypes.data, len(lens), None, 0)
     if n < 0:
         raise FfwdError("attention_items failed")
-    out = np.zeros((max(n, 1), 6), np.int32)
-    got = L.ffwd_b200_attention_items(int(causal), n_heads, n_kv_heads, offs.ctypes.data,
-                                      len(lens), out.ctypes.data, n)
-    if got != n:
+    out = np.zeros((max(n, 1), 7), np.int32)
+    got = L.ffwd_b200_attention_items(int(causal), int(windows), n_heads, n_kv_heads,
+                                      offs.ctypes.data, len(lens), out.ctypes.data, n)
+    if got < 0 or got > n:
         raise FfwdError("attention_items failed")
-    return out[:n]
+    return out[:got]
 
 
 def gemm_bf16(x_ptr, w_ptr, y_ptr, M, N, K, bn=256, x_lo_ptr=None, w_lo_ptr=None):

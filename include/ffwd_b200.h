@@ -309,10 +309,13 @@ FFWD_B200_API int ffwd_b200_lpt_partition(const double *cost, int n, int n_parts
 
 /* Attention work list of a packed batch (host; the list the forward builds),
  * exposed for tests: pairs of 128-row query blocks sharing a key/value head.
- * offsets: [batch + 1] row offsets.  Writes up to cap items as 6 ints each
- * (seq, qt0, h0, qt1, h1, key tiles) when items is non-NULL; returns the item
- * count, -1 on bad arguments or when cap is too small. */
-FFWD_B200_API int ffwd_b200_attention_items(int causal, int n_heads, int n_kv_heads,
+ * windows != 0: neighbouring sequences of at most 128 rows share items (the
+ * list of the 16-bit plans).  offsets: [batch + 1] row offsets.  With items
+ * NULL returns an upper bound of the count; else writes up to cap items as 7
+ * ints each (seq, qt0, h0, qt1, h1, key tiles, window sequences: 0 for a
+ * single-sequence item) and returns the count; -1 on bad arguments or when cap
+ * is too small. */
+FFWD_B200_API int ffwd_b200_attention_items(int causal, int windows, int n_heads, int n_kv_heads,
                                             const int *offsets, int batch, int *items, int cap);
 
 /* Operator-level entry for tests: Y = X W^T with the tcgen05 GEMM on device

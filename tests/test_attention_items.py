@@ -21,7 +21,8 @@ def tiles(L, t):
 def check_tc_cover(lens, heads, kv, hd, causal):
     it = native.attention_items(lens, heads, kv, causal=causal)
     seen = collections.Counter()
-    for seq, qt0, h0, qt1, h1, cost in it:
+    for seq, qt0, h0, qt1, h1, cost, nseq in it:
+        assert nseq == 0
         nq = tiles(lens[seq], 128)
         blocks = [(qt0, h0)] + ([(qt1, h1)] if qt1 >= 0 else [])
         for qt, h in blocks:
@@ -56,6 +57,65 @@ def test_tensor_core_items_cover_once_random(lens, layout, causal):
     check_tc_cover(lens, *layout, causal)
 
 
+def check_window_cover(lens, heads, kv, causal):
+    """The 16-bit plans' list: sequences of 1..128 rows that are neighbours in
+    the packed layout share window items; every (head, row) of every sequence
+    is covered exactly once; windows come after the single-sequence items."""
+    rep = heads // kv
+    offs = np.concatenate([[0], np.cumsum(lens)])
+    it = native.attention_items(lens, heads, kv, causal=causal, windows=True)
+    rows = collections.Counter()
+    seen_window = False
+    cap = 128 if rep >= 2 else 256
+    for seq, qt0, h0, qt1, h1, cost, nseq in it:
+        blocks = [(qt0, h0)] + ([(qt1, h1)] if qt1 >= 0 else [])
+        assert len({h * kv // heads for _, h in blocks}) == 1
+        if nseq == 0:
+            assert not seen_window and lens[seq] > 128
+            base, L = offs[seq], lens[seq]
+            nq = tiles(L, 128)
+            assert cost == (max(q for q, _ in blocks) + 1 if causal else nq)
+        else:
+            seen_window = True
+            members = list(range(seq, seq + nseq))
+            assert all(1 <= lens[m] <= 128 for m in members)
+            base, L = offs[seq], offs[seq + nseq] - offs[seq]
+            assert L <= cap
+            assert cost == (1 if rep >= 2 else tiles(L, 128))
+            if rep >= 2:
+                assert qt0 == 0 and (qt1 < 0 or (qt1 == 0 and h1 == h0 + 1))
+            else:
+                assert qt0 == 0 and (qt1 == 1 and h1 == h0) == (L > 128)
+        for qt, h in blocks:
+            for r in range(base + qt * 128, base + min(qt * 128 + 128, L)):
+                rows[(h, r)] += 1
+    want = {(h, r) for h in range(heads) for r in range(int(offs[-1]))}
+    assert set(rows) == want and max(rows.values()) == 1
+    # a run of short neighbours is cut only where the next one does not fit
+    win = [(s, n) for s, *_, n in it if n > 0]
+    starts = sorted({s for s, _ in win})
+    for s in starts:
+        n = dict(win)[s]
+        e = s + n
+        if e < len(lens) and 1 <= lens[e] <= 128:
+            assert offs[e + 1] - offs[s] > cap
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("heads,kv", [(16, 8), (32, 8), (12, 12), (14, 2)])
+def test_window_items_cover_once(causal, heads, kv):
+    check_window_cover(LENS + [30, 40, 50, 128, 1, 100, 100, 3000, 60], heads, kv, causal)
+
+
+@settings(max_examples=60, deadline=None)
+@given(lens=st.lists(st.one_of(st.integers(1, 140), st.integers(1, 3000)), min_size=1,
+                     max_size=40),
+       layout=st.sampled_from([(16, 8), (32, 8), (12, 12), (16, 16), (14, 2)]),
+       causal=st.booleans())
+def test_window_items_cover_once_random(lens, layout, causal):
+    check_window_cover(lens, *layout, causal)
+
+
 def test_tensor_core_item_order():
     """Longest sequence first; within a sequence the items of one key/value
     head are contiguous, heaviest query tile first."""
@@ -77,7 +137,8 @@ def test_tensor_core_item_order():
 def test_bad_arguments():
     L = native.lib()
     offs = np.array([0, 4], np.int32)
-    assert L.ffwd_b200_attention_items(1, 12, 5, offs.ctypes.data, 1, None, 0) == -1
-    out = np.zeros((1, 6), np.int32)
+    assert L.ffwd_b200_attention_items(1, 0, 12, 5, offs.ctypes.data, 1, None, 0) == -1
+    out = np.zeros((1, 7), np.int32)
     # 16 heads over 8 kv heads, 4 tokens: 8 items do not fit in 1
-    assert L.ffwd_b200_attention_items(1, 16, 8, offs.ctypes.data, 1, out.ctypes.data, 1) == -1
+    assert L.ffwd_b200_attention_items(1, 0, 16, 8, offs.ctypes.data, 1, out.ctypes.data, 1) == -1
+    assert L.ffwd_b200_attention_items(1, 1, 16, 8, offs.ctypes.data, 1, out.ctypes.data, 1) == -1

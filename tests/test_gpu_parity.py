@@ -168,7 +168,14 @@ def test_max_tokens_chunking_matches(model_root):
         chunked = native.B200Model(d, gemm_mode="bf16").encode_batch(seqs)
     finally:
         native.lib().ffwd_b200_set_max_tokens(262144)
-    assert np.array_equal(whole, chunked)
+    # Sequences longer than one query tile have their own attention items, so
+    # their rows do not depend on the rest of the forward; shorter ones share
+    # items with their neighbours (windows), which a different chunking
+    # regroups: equal to rounding.
+    lens = np.array([len(q) for q in seqs])
+    assert (lens > 128).any() and (lens <= 128).any()
+    assert np.array_equal(whole[lens > 128], chunked[lens > 128])
+    assert cos_rows(whole, chunked).min() >= 0.99999
 
 
 def test_public_api_matches_abi(model_root):
