@@ -110,6 +110,7 @@ __device__ __forceinline__ void arrive_leader(uint64_t *bar) {
 // clipped by the tensor map.
 struct TmaSink {
     static constexpr bool kAllRows = true;  // every row takes part in the barriers
+    static constexpr bool kFastGelu = true;  // 16-bit outputs: GELU through ex2
     static constexpr bool kHalfRope = true;  // single-pass bf16 only: RoPE from f16 tables
     const GemmParams &p;
     const CUtensorMap *map;

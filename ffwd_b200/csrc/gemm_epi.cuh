@@ -21,6 +21,29 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.0f + tanhf(inner));
 }
 
+// GELU for 16-bit outputs (the single-pass two-SM GEMM), as x * sigmoid(u) =
+// x / (1 + 2^-u'), two MUFU operations instead of erff / tanhf:
+// - erf form: 0.5 (1 + erf(x / sqrt 2)) = sigmoid(q(x)) with q an odd quintic
+//   fitted here (weighted least squares on |x| <= 8.5): erf matched to 3.7e-5,
+//   GELU to 5.5e-5 absolute, far below the 16-bit output's rounding; |x| is
+//   clamped to 8.5 inside q (beyond, GELU is x or 0 in f32);
+// - tanh form: 0.5 (1 + tanh(v)) = sigmoid(2 v) exactly, v = sqrt(2 / pi) (x +
+//   0.044715 x^3) as in the reference's gelu_new.
+// The exact plans keep erff / tanhf (their outputs feed f32 comparisons).
+__device__ __forceinline__ float gelu_erf_fast(float x) {
+    const float c = fminf(fmaxf(x, -8.5f), 8.5f);
+    const float c2 = c * c;
+    // -2 log2(e) q(c): the exponent of 2 in the sigmoid's denominator.
+    const float e = c * fmaf(fmaf(9.1122725e-4f, c2, -0.10617733f), c2, -2.3017271f);
+    return __fdividef(x, 1.0f + ex2_approx(e));
+}
+
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+    // -2 log2(e) sqrt(2 / pi) = -2.3022082; times 0.044715 = -0.1029432
+    const float e = x * fmaf(-0.1029432f, x * x, -2.3022082f);
+    return __fdividef(x, 1.0f + ex2_approx(e));
+}
+
 __device__ __forceinline__ void add_bias32(float (&v)[32], const float *bias, int col) {
     const float4 *b4 = reinterpret_cast<const float4 *>(bias + col);
 #pragma unroll
@@ -92,6 +115,7 @@ __device__ __forceinline__ void store_row32(const GemmParams &p, int row, int co
 // Writes each thread's row segments straight to global memory.
 struct DirectSink {
     static constexpr bool kAllRows = false;  // rows past M skip their work
+    static constexpr bool kFastGelu = false;  // erff / tanhf (also the exact plans)
     static constexpr bool kHalfRope = false;  // RoPE from the f32 tables
     const GemmParams &p;
     int grow;
@@ -130,7 +154,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
             if (!Sink::kAllRows && !valid) continue;
             const int col = n0 + c * 32;
             if (p.bias) add_bias32(v, p.bias, col);
-            if constexpr (EPI == kEpiGelu) {
+            if constexpr (EPI == kEpiGelu && Sink::kFastGelu) {
+                if (p.gelu_tanh) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_fast(v[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = gelu_erf_fast(v[i]);
+                }
+            } else if constexpr (EPI == kEpiGelu) {
                 if (p.gelu_tanh) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
