@@ -145,6 +145,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_sh;
+    // Nothing above touches data of other kernels; wait for the stream's
+    // previous kernel, then let the next one start launching.
+    griddep_wait();
+    griddep_launch();
 
     uint8_t *sQ = smem + C::OFF_Q;
     uint8_t *sRing = smem + C::OFF_RING;
@@ -642,6 +646,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_sh;
+    // Nothing above touches data of other kernels; wait for the stream's
+    // previous kernel, then let the next one start launching.
+    griddep_wait();
+    griddep_launch();
 
     if (warp == kSplitProducerWarp) {
         if (lane == 0) {
@@ -907,7 +915,9 @@ int attention_tc_launch(const CUtensorMap *qkv_map, const AttnParams &p, cudaStr
     do {                                                                                     \
         e = set_smem_once<attn_tc_kernel<DD, FF>>(AttnCfg<DD>::SMEM);                        \
         if (e != cudaSuccess) return e;                                                      \
-        attn_tc_kernel<DD, FF><<<grid, kAttnThreads, AttnCfg<DD>::SMEM, stream>>>(*qkv_map, p); \
+        e = launch_k(attn_tc_kernel<DD, FF>, grid, dim3(kAttnThreads), AttnCfg<DD>::SMEM, stream, \
+                     *qkv_map, p);                                                           \
+        if (e != cudaSuccess) return e;                                                      \
     } while (0)
     const bool f16 = p.f16 != 0;
     switch (p.head_dim) {
@@ -936,8 +946,9 @@ int attention_split_launch(const CUtensorMap *qkv_hi_map, const CUtensorMap *qkv
     do {                                                                                   \
         e = set_smem_once<attn_split_kernel<DD>>(SplitCfg<DD>::SMEM);                      \
         if (e != cudaSuccess) return e;                                                    \
-        attn_split_kernel<DD><<<grid, kSplitThreads, SplitCfg<DD>::SMEM, stream>>>(         \
-            *qkv_hi_map, *qkv_lo_map, p);                                                  \
+        e = launch_k(attn_split_kernel<DD>, grid, dim3(kSplitThreads), SplitCfg<DD>::SMEM,  \
+                     stream, *qkv_hi_map, *qkv_lo_map, p);                                 \
+        if (e != cudaSuccess) return e;                                                    \
     } while (0)
     switch (p.head_dim) {
     case 32: ATTN_SPLIT(32); break;

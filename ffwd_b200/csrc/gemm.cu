@@ -96,6 +96,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_sh;
+    // Nothing above touches data of other kernels; wait for the stream's
+    // previous kernel, then let the next one start launching.
+    griddep_wait();
+    griddep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -229,8 +233,8 @@ int launch_t(const CUtensorMap *a, const CUtensorMap *a_lo, const CUtensorMap *b
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + BM - 1) / BM) * (p.N / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, kThreads, C::SMEM, stream>>>(*a, a_lo ? *a_lo : *a, *b, b_lo ? *b_lo : *b, p);
-    return cudaGetLastError();
+    return launch_k(kern, dim3(grid), dim3(kThreads), C::SMEM, stream, *a, a_lo ? *a_lo : *a, *b,
+                    b_lo ? *b_lo : *b, p);
 }
 
 template <int BN, int PASSES>

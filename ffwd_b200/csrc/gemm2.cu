@@ -279,6 +279,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();  // both CTAs' barriers initialised before any remote use
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_sh;
+    // Nothing above touches data of other kernels; wait for the stream's
+    // previous kernel, then let the next one start launching.
+    griddep_wait();
+    griddep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -402,8 +406,8 @@ int launch2(const CUtensorMap *a, const CUtensorMap *b_half, const CUtensorMap *
     int grid = 2 * tiles;
     const int cap = num_sms & ~1;
     if (grid > cap) grid = cap;
-    kern<<<grid, kThreads, Cfg2<EPI>::SMEM, stream>>>(*a, *b_half, *out, p);
-    return cudaGetLastError();
+    return launch_k(kern, dim3(grid), dim3(kThreads), Cfg2<EPI>::SMEM, stream, *a, *b_half, *out,
+                    p);
 }
 
 }  // namespace

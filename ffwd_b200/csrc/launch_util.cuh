@@ -3,6 +3,8 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 #include <cuda_runtime.h>
 
 namespace fb {
@@ -21,6 +23,34 @@ cudaError_t set_smem_once(int bytes) {
     e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
     return e;
+}
+
+// Launch with programmatic stream serialization (the kernel must call
+// griddep_wait before touching global data, see ptx.cuh), so the launch and
+// set-up of kernel k + 1 overlap the tail of kernel k.  FFWD_B200_PDL=0 makes
+// it a normal launch (A/B comparisons).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("FFWD_B200_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace fb

@@ -53,6 +53,23 @@ __device__ __forceinline__ bool elect_one_sync() {
     return pred != 0;
 }
 
+// ----------------------------------------------------------------- dependent launch
+// For kernels launched with programmatic stream serialization (launch_util.cuh
+// launch_k): griddep_wait blocks until the stream's previous kernel has
+// completed and its memory operations are visible (a no-op after a normal
+// launch), so every access to data another kernel produces or reads comes
+// after it; griddep_launch lets the stream's next kernel start launching, its
+// CTAs taking SMs as this kernel's CTAs exit and doing their set-up before
+// their own griddep_wait.
+
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ----------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {

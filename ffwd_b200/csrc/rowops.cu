@@ -3,6 +3,7 @@
 // kernel uses the same lane -> column mapping, so a thread only re-reads what
 // it wrote itself.
 #include "rowops.cuh"
+#include "launch_util.cuh"
 #include "ptx.cuh"
 
 namespace fb {
@@ -163,6 +164,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 template <int NC>
 __global__ void __launch_bounds__(kRowWarps * 32)
     rmsnorm_kernel(const float *x, int T, int H, const float *w, float eps, RowOut xn) {
+    griddep_wait();  // x comes from the stream's previous kernel
+    griddep_launch();
     const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= T) return;
@@ -295,6 +298,8 @@ __device__ __forceinline__ void layernorm_row(float *xr, int H, int lane, const 
 template <int NC>
 __global__ void __launch_bounds__(kRowWarps * 32)
     layernorm_kernel(float *x, int T, int H, const float *g, const float *b, float eps, RowOut xb) {
+    griddep_wait();  // x comes from the stream's previous kernel
+    griddep_launch();
     const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= T) return;
@@ -610,19 +615,23 @@ int embed_ln_launch(const int *ids, const int *pos, int T, const void *table, in
 int rmsnorm_launch(const float *x, int T, int H, const float *w, float eps, RowOut xn,
                    cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-#define K(NC) rmsnorm_kernel<NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, w, eps, xn)
+    cudaError_t e = cudaSuccess;
+#define K(NC) \
+    e = launch_k(rmsnorm_kernel<NC>, dim3(row_blocks(T)), dim3(kRowWarps * 32), 0, s, x, T, H, w, eps, xn)
     FFWD_ROW_DISPATCH(H, K)
 #undef K
-    return cudaGetLastError();
+    return e;
 }
 
 int layernorm_launch(float *x, int T, int H, const float *g, const float *b, float eps,
                      RowOut xb, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-#define K(NC) layernorm_kernel<NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(x, T, H, g, b, eps, xb)
+    cudaError_t e = cudaSuccess;
+#define K(NC) \
+    e = launch_k(layernorm_kernel<NC>, dim3(row_blocks(T)), dim3(kRowWarps * 32), 0, s, x, T, H, g, b, eps, xb)
     FFWD_ROW_DISPATCH(H, K)
 #undef K
-    return cudaGetLastError();
+    return e;
 }
 
 int pool_launch(const float *x, const int *offsets, int batch, int H, int mode,
