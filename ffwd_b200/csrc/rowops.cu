@@ -91,6 +91,8 @@ template <bool BF16, int NC>
 __global__ void __launch_bounds__(kRowWarps * 32)
     embed_rms_kernel(const int *ids, int T, const void *table, int vocab, int H, float *x,
                      const float *w, float eps, RowOut xn, int *err) {
+    griddep_wait();  // inputs come from the stream's previous kernel
+    griddep_launch();
     const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= T) return;
@@ -322,6 +324,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     embed_ln_kernel(const int *ids, const int *pos, int T, const void *table, int vocab,
                     const float *pos_table, const float *type0, const float *g, const float *b,
                     int H, float eps, float *x, RowOut xb, int *err) {
+    griddep_wait();  // inputs come from the stream's previous kernel
+    griddep_launch();
     const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= T) return;
@@ -384,6 +388,8 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 __global__ void __launch_bounds__(kPoolThreads)
     pool_kernel(const float *x, const int *starts, const int *ends, int H, int mode,
                 const float *norm_w, float eps, int normalize, float *out, int *err) {
+    griddep_wait();  // inputs come from the stream's previous kernel
+    griddep_launch();
     __shared__ float red[kPoolThreads / 32];
     const int b = blockIdx.x;
     const int s = starts[b], e = ends[b];
@@ -448,6 +454,8 @@ constexpr int kMeanThreads = 1024;
 __global__ void __launch_bounds__(kMeanThreads)
     pool_mean_kernel(const float *x, const int *starts, const int *ends, int H, int normalize,
                      float *out, int *err) {
+    griddep_wait();  // inputs come from the stream's previous kernel
+    griddep_launch();
     __shared__ float4 part[kMeanThreads];
     __shared__ float red[kMeanThreads / 32];
     __shared__ float inv_sh;
@@ -583,16 +591,17 @@ inline int row_groups(int H) { return H <= 256 ? 1 : H <= 512 ? 2 : H <= 768 ? 3
 int embed_rms_launch(const int *ids, int T, const void *table, int table_bf16, int vocab, int H,
                      float *x, const float *w, float eps, RowOut xn, int *err, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-#define K(NC)                                                                                   \
-    if (table_bf16)                                                                             \
-        embed_rms_kernel<true, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(ids, T, table, vocab, \
-                                                                            H, x, w, eps, xn, err); \
-    else                                                                                        \
-        embed_rms_kernel<false, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(                   \
-            ids, T, table, vocab, H, x, w, eps, xn, err)
+    cudaError_t e = cudaSuccess;
+#define K(NC)                                                                                \
+    e = table_bf16 ? launch_k(embed_rms_kernel<true, NC>, dim3(row_blocks(T)),               \
+                              dim3(kRowWarps * 32), 0, s, ids, T, table, vocab, H, x, w, eps, \
+                              xn, err)                                                       \
+                   : launch_k(embed_rms_kernel<false, NC>, dim3(row_blocks(T)),              \
+                              dim3(kRowWarps * 32), 0, s, ids, T, table, vocab, H, x, w, eps, \
+                              xn, err)
     FFWD_ROW_DISPATCH(H, K)
 #undef K
-    return cudaGetLastError();
+    return e;
 }
 
 int embed_ln_launch(const int *ids, const int *pos, int T, const void *table, int table_bf16,
@@ -600,16 +609,17 @@ int embed_ln_launch(const int *ids, const int *pos, int T, const void *table, in
                     const float *b, int H, float eps, float *x, RowOut xb, int *err,
                     cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
+    cudaError_t e = cudaSuccess;
 #define K(NC)                                                                                \
-    if (table_bf16)                                                                          \
-        embed_ln_kernel<true, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(                  \
-            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err);          \
-    else                                                                                     \
-        embed_ln_kernel<false, NC><<<row_blocks(T), kRowWarps * 32, 0, s>>>(                 \
-            ids, pos, T, table, vocab, pos_table, type0, g, b, H, eps, x, xb, err)
+    e = table_bf16 ? launch_k(embed_ln_kernel<true, NC>, dim3(row_blocks(T)),                \
+                              dim3(kRowWarps * 32), 0, s, ids, pos, T, table, vocab,         \
+                              pos_table, type0, g, b, H, eps, x, xb, err)                    \
+                   : launch_k(embed_ln_kernel<false, NC>, dim3(row_blocks(T)),               \
+                              dim3(kRowWarps * 32), 0, s, ids, pos, T, table, vocab,         \
+                              pos_table, type0, g, b, H, eps, x, xb, err)
     FFWD_ROW_DISPATCH(H, K)
 #undef K
-    return cudaGetLastError();
+    return e;
 }
 
 int rmsnorm_launch(const float *x, int T, int H, const float *w, float eps, RowOut xn,
@@ -640,12 +650,10 @@ int pool_launch(const float *x, const int *offsets, int batch, int H, int mode,
     if (batch <= 0) return cudaSuccess;
     if (H > kPoolThreads * kPoolMaxCols) return cudaErrorInvalidValue;
     if (mode == 0 && !norm_w && H % 4 == 0)
-        pool_mean_kernel<<<batch, kMeanThreads, 0, s>>>(x, offsets, offsets + 1, H, normalize, out,
-                                                        err);
-    else
-        pool_kernel<<<batch, kPoolThreads, 0, s>>>(x, offsets, offsets + 1, H, mode, norm_w, eps,
-                                                    normalize, out, err);
-    return cudaGetLastError();
+        return launch_k(pool_mean_kernel, dim3(batch), dim3(kMeanThreads), 0, s, x, offsets,
+                        offsets + 1, H, normalize, out, err);
+    return launch_k(pool_kernel, dim3(batch), dim3(kPoolThreads), 0, s, x, offsets, offsets + 1, H,
+                    mode, norm_w, eps, normalize, out, err);
 }
 
 int encode_rows_launch(const float *emb, int B, int H, int dims, int renorm, int enc, void *out,
