@@ -281,3 +281,35 @@ def test_qwen3_8b_shape_long_documents(model_root):
     check(m.encode_batch(seqs), ref, False)
     trunc = m.encode_batch_as(seqs, 1024, True, "f32")
     check(trunc, of.truncate_renormalize(ref, 1024), False)
+
+
+def test_dependent_launch_off_matches(model_root, tmp_path):
+    """Programmatic dependent launch changes only when kernels start, not what
+    they compute: the same batches with FFWD_B200_PDL=0 (ordinary launches, in
+    a child process, since the switch is read once per process) give the same
+    bits, for a decoder and an encoder."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cases = [("qwen3-2l", "bf16", 300, 17), ("bge-bf16-2l", "bf16", 200, 5), ("minilm-2l", "f32", 128, 3)]
+    want = []
+    for key, mode, max_len, seed in cases:
+        d = synth.ensure_model(small_spec(key), model_root)
+        want.append(model(d, mode).encode_batch(small_batch(key, n=6, max_len=max_len, seed=seed)))
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = [{root!r}, {os.path.join(root, 'tests')!r}]\n"
+        "from ffwd_b200 import native, synth\n"
+        "from helpers import small_spec, small_batch\n"
+        f"for i, (key, mode, max_len, seed) in enumerate({cases!r}):\n"
+        f"    d = synth.ensure_model(small_spec(key), {model_root!r})\n"
+        "    m = native.B200Model(d, gemm_mode=mode)\n"
+        "    out = m.encode_batch(small_batch(key, n=6, max_len=max_len, seed=seed))\n"
+        f"    np.save({str(tmp_path)!r} + f'/out{{i}}.npy', out)\n"
+    )
+    subprocess.run([sys.executable, "-c", code], env={**os.environ, "FFWD_B200_PDL": "0"},
+                   check=True, cwd=root, timeout=600)
+    for i, w in enumerate(want):
+        assert np.array_equal(w, np.load(tmp_path / f"out{i}.npy"))
