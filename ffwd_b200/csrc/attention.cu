@@ -259,25 +259,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 return item_sh[k % kItemSlots] < 0 ? 0 : geo_sh[k % kItemSlots].n_kt;
             };
             // S_b(g) for block b of item k (Q buffer k & 1) against K(g).
+            const uint32_t dhi = (uint32_t)(dQ >> 32);
+            const uint32_t qlo = (uint32_t)dQ, klo = (uint32_t)dRingK, vlo = (uint32_t)dRingV;
             auto issue_s = [&](int b, int k, int g) {
-                const uint64_t dK = dRingK + (uint64_t)((((2 * g) % C::RING) * C::TILE_BYTES) >> 4);
-                const uint64_t dQb = dQ + (uint64_t)((((k & 1) * 2 + b) * C::TILE_BYTES) >> 4);
+                const uint32_t dK = klo + (uint32_t)((((2 * g) % C::RING) * C::TILE_BYTES) >> 4);
+                const uint32_t dQb = qlo + (uint32_t)((((k & 1) * 2 + b) * C::TILE_BYTES) >> 4);
                 const uint32_t d = tmem_base + b * kTile;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(d, dQb + kk_off(kk), dK + kk_off(kk), IDESC_S, kk != 0);
+                    umma_f16_lo(d, dQb + (uint32_t)kk_off(kk), dK + (uint32_t)kk_off(kk), dhi,
+                                IDESC_S, kk != 0);
                 umma_commit(&s_full[b]);
             };
             // O_b (+)= P_b(g) V(g); P_b sits in the first half of S_b's columns.
             auto issue_pv = [&](int b, int g, bool first) {
-                const uint64_t dV =
-                    dRingV + (uint64_t)((((2 * g + 1) % C::RING) * C::TILE_BYTES) >> 4);
+                const uint32_t dV =
+                    vlo + (uint32_t)((((2 * g + 1) % C::RING) * C::TILE_BYTES) >> 4);
                 const uint32_t tP = tmem_base + b * kTile;
                 const uint32_t dO = tmem_base + 256 + b * 128;
 #pragma unroll
                 for (int kk = 0; kk < kTile / 16; ++kk)
-                    umma_f16_ts(dO, tP + kk * 8, dV + (uint64_t)((kk * 16 * C::ROWB) >> 4), IDESC_O,
-                                !first || kk != 0);
+                    umma_f16_ts_lo(dO, tP + kk * 8, dV + (uint32_t)((kk * 16 * C::ROWB) >> 4), dhi,
+                                   IDESC_O, !first || kk != 0);
             };
             int k = 0, g = 0;  // local item, global tile counter
             int n = next_item(0);
