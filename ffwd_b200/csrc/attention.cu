@@ -473,12 +473,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 const float m_old = m_used;
                 if (j == 0 || rescale) m_used = m_new;
                 // P over the first 64 columns of the score buffer: key 2c, 2c + 1 in
-                // column c.  (Moving a share of the exponentials to an FMA-pipe
-                // polynomial was measured slower: the softmax warps are bound by
-                // instruction issue, not by the MUFU unit.)
-                // Key pairs are scaled with one packed f32x2 FMA: the softmax warps
-                // are bound by instruction issue.  (A packed add for the row sum
-                // was measured to cost registers: it spills.)
+                // column c.  Key pairs are scaled with one packed f32x2 FMA.  (Moving
+                // a share of the exponentials to an FMA-pipe polynomial was measured
+                // slower, and with no exponentials at all the kernel is no faster:
+                // the MMA-issuing thread, not the softmax, sets the pace.  A packed
+                // add for the row sum was measured to cost registers: it spills.)
                 float2 la[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
                 // (m_used is -inf only while the row has seen no visible key: then
                 // every score is -inf and 0 keeps P at 0.)
