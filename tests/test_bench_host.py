@@ -32,3 +32,21 @@ def test_flops_per_token_matches_survey():
     total, lin, attn = bench.flops_per_token(spec, seqs)
     assert abs(lin / 1e6 - 880.8) < 0.5
     assert attn > 0 and abs(total - lin - attn) < 1
+
+
+def test_config_sweep_covers_every_baseline_config():
+    """`bench.py --configs` times every BASELINE configuration (the 8B shape at
+    reduced depth, with the same per-layer shapes) in the GEMM mode the
+    configuration names."""
+    from ffwd_b200 import synth
+
+    names = {name for name, _, _, _ in bench.SWEEP}
+    assert names == set(synth.CONFIGS)
+    modes = {name: mode for name, mode, _, _ in bench.SWEEP}
+    assert modes["minilm"] == "f32" and modes["bge-base"] == "f32"
+    assert all(modes[n] == "bf16" for n in ("bge-base-bf16", "xlmr-large", "qwen3-0.6b", "qwen3-8b"))
+    for name, _, _, over in bench.SWEEP:
+        spec = synth.spec(name, **over) if over else synth.CONFIGS[name]
+        base = synth.CONFIGS[name]
+        assert (spec.hidden, spec.n_heads, spec.n_kv_heads, spec.head_dim, spec.intermediate) == \
+            (base.hidden, base.n_heads, base.n_kv_heads, base.head_dim, base.intermediate)
