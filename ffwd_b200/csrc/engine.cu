@@ -188,7 +188,7 @@ struct Workspace {
 // re-issued for timing).
 struct FwdState {
     int T = 0, B = 0, n_items = 0;
-    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv, m_qkv_lo, m_kv;
+    CUtensorMap m_xb, m_xb_lo, m_att, m_att_lo, m_h, m_h_lo, m_qkv, m_qkv_lo;
     AttnParams ap{};
 };
 
@@ -843,10 +843,7 @@ int make_act_maps(const ffwd_b200_ctx *ctx, FwdState &fs, const Workspace &w, in
                        make_map(&fs.m_h_lo, w.hmid_lo, T, I, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B)
                    ? -1
                    : 0;
-    return make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, hb, sw) ||
-                   make_map(&fs.m_kv, w.qkv, T, qkv_dim, 64, hb, sw)
-               ? -1
-               : 0;
+    return make_map(&fs.m_qkv, w.qkv, T, qkv_dim, 128, hb, sw) ? -1 : 0;
 }
 
 int embed_step(ffwd_b200_ctx *ctx, Device &D, const FwdState &fs, Workspace &w);
