@@ -26,7 +26,7 @@ def test_cpu_info():
     assert info["nproc"] >= 1 and 1 <= info["physical_cores"] <= info["nproc"]
 
 
-def test_flops_per_token_matches_survey():
+def test_flops_per_token_of_the_bench_model():
     # Qwen3-0.6B: 880.8 MFLOP/token in the projections (2 x MAC, 28 layers)
     spec, seqs = bench.workload(0)
     total, lin, attn = bench.flops_per_token(spec, seqs)
