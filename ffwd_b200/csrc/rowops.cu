@@ -168,9 +168,13 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     rmsnorm_kernel(const float *x, int T, int H, const float *w, float eps, RowOut xn) {
     griddep_wait();  // x comes from the stream's previous kernel
     griddep_launch();
-    const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    // Last rows first: the residual GEMM before this kernel wrote them last
+    // (they are likely still in L2), and the GEMM after it starts with the
+    // first rows, which this kernel writes last.
+    const int rf = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= T) return;
+    if (rf >= T) return;
+    const int row = T - 1 - rf;
     const float *xr = x + (size_t)row * H;
     float ss = 0.0f;
     if constexpr (NC > 0) {
@@ -302,9 +306,11 @@ __global__ void __launch_bounds__(kRowWarps * 32)
     layernorm_kernel(float *x, int T, int H, const float *g, const float *b, float eps, RowOut xb) {
     griddep_wait();  // x comes from the stream's previous kernel
     griddep_launch();
-    const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    // Last rows first, as in rmsnorm_kernel (L2 reuse with the GEMMs around it).
+    const int rf = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= T) return;
+    if (rf >= T) return;
+    const int row = T - 1 - rf;
     float *xr = x + (size_t)row * H;
     if constexpr (NC > 0) {
         float v[NC][8];
